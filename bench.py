@@ -1,0 +1,416 @@
+"""Benchmark of the FP8 decode GEMV hot path on B200.
+
+One step = one pass of BASELINE config 1: the FP8-weight GEMV at
+(N, K) = (28672, 4096) gate_up, (4096, 14336) down, (6144, 4096) QKV, each at
+M = 1, 2, 4, 8 tokens (12 launches), e4m3 weights with fp32 per-channel
+scales, fp16 activations, seeded synthetic data.  Two weight sets alternate
+between steps (402 MB > 126 MB L2), so every launch streams its weights from
+HBM.
+
+  value       whole-job HBM GB/s (algorithmic bytes of all ranks / max-over-
+              ranks device time), one CUDA-graph replay per step, inputs
+              resident in HBM
+  e2e         the same metric through the public torch op, eager, with the
+              step's activations copied host->device from pinned memory and
+              the outputs read back device->host inside the timed region
+  roofline    the GEMV kernel: algorithmic bytes / CUDA-event time of its
+              launches vs the measured HBM copy bandwidth
+  cpu_baseline  the CPU oracle (torch fp32 dequant-then-matmul, the
+              reference tests' oracle) on this host's cores, a bounded sample
+
+`--impl reference` times the reference's CPU path (the oracle port: the
+reference's own kernels are Intel-GPU-only and cannot run here) on the same
+workload, rank 0 only.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+(N > 1 under torch.distributed.run: one rank per GPU, each rank runs the
+same independent GEMV sweep: weak scaling, no collective on the data path.)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SHAPES = [("gate_up", 28672, 4096), ("down", 4096, 14336), ("qkv", 6144, 4096)]
+MS = [1, 2, 4, 8]
+CALLS = [(name, N, K, M) for M in MS for (name, N, K) in SHAPES]
+METRIC = "FP8 GEMV HBM GB/s, config 1 sweep (gate_up/down/qkv x M=1,2,4,8)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def call_bytes(M: int, N: int, K: int) -> int:
+    """Algorithmic bytes of one GEMV: weights + activations + fp32 scales + outputs."""
+    return N * K + 2 * M * K + 4 * N + 2 * M * N
+
+
+STEP_BYTES = sum(call_bytes(M, N, K) for (_, N, K, M) in CALLS)
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per config-1 step from the committed ncu summary, if present."""
+    f = ROOT / "profiles" / "gemv_fp8_config1.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_step:"):
+            return float(line.split(":", 1)[1].strip())
+    return None
+
+
+# ---- clocks sampling ------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.rows: list[list[str]] = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.3)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        for r in self.rows:
+            try:
+                sm.append(float(r[0]))
+                mx = max(mx, float(r[1]))
+                for name, v in zip(self.NAMES, r[3:7]):
+                    if v.lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---- distributed plumbing --------------------------------------------------------------
+
+def dist_init(n_gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch with torch.distributed.run")
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- our arm ------------------------------------------------------------------------
+
+def build_sets(dev, n_sets: int = 2):
+    from esimd_learning_b200.workloads import make_fp8_weight
+
+    gen = torch.Generator().manual_seed(0)
+    sets = []
+    for s in range(n_sets):
+        ws = {}
+        for name, N, K in SHAPES:
+            wq, sc = make_fp8_weight(N, K, gen)
+            ws[name] = (wq.to(dev), sc.to(dev))
+        sets.append(ws)
+    xs = {}
+    for name, N, K in SHAPES:
+        for M in MS:
+            xs[(name, M)] = torch.randn(M, K, generator=gen).to(torch.float16).to(dev)
+    ys = {(name, M): torch.empty(M, N, dtype=torch.float16, device=dev)
+          for (name, N, K, M) in CALLS}
+    return sets, xs, ys
+
+
+def run_ours(args, rank, world, local):
+    import esimd_learning_b200 as ops
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    sets, xs, ys = build_sets(dev)
+
+    def step():
+        # the weight set alternates with M, so two uses of one set are always
+        # separated by > 126 MB of other weights
+        for (name, N, K, M) in CALLS:
+            wq, sc = sets[MS.index(M) % 2][name]
+            ops.esimd_gemv_fp8_pern(xs[(name, M)], wq, sc, ys[(name, M)], N, K)
+
+    st = torch.cuda.Stream(dev)
+    with torch.cuda.stream(st):
+        step()  # warm (module load) outside capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            step()
+    torch.cuda.synchronize()
+
+    # --- per-call kernel times (CUDA events on the launching stream, L2 flushed) ---
+    per_call = {}
+    reps = 10
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(st):
+        for (name, N, K, M) in CALLS:
+            evs = []
+            for r in range(reps + 2):
+                wq, sc = sets[r % 2][name]
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                ops.esimd_gemv_fp8_pern(xs[(name, M)], wq, sc, ys[(name, M)], N, K)
+                e1.record(st)
+                evs.append((e0, e1))
+            torch.cuda.synchronize()
+            ts = [a.elapsed_time(b) * 1e3 for a, b in evs[2:]]
+            per_call[f"{name}_M{M}"] = statistics.median(ts)
+    del flush
+
+    # --- timed region: graph replays ---
+    for i in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            for i in range(args.steps):
+                graph.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_total = max_over_ranks(e0.elapsed_time(e1), world)
+    ms_step = ms_total / args.steps
+    value = STEP_BYTES * world / (ms_step * 1e-3) / 1e9
+
+    # --- e2e: public torch op, eager, host buffers, copies inside the timed region ---
+    hx = {k: v.cpu().pin_memory() for k, v in xs.items()}
+    hy = {k: torch.empty(v.shape, dtype=v.dtype).pin_memory() for k, v in ys.items()}
+    h2d = sum(v.numel() * v.element_size() for v in hx.values())
+    d2h = sum(v.numel() * v.element_size() for v in hy.values())
+    e2e_steps = max(3, min(args.steps, 200))
+
+    def e2e_step():
+        for (name, N, K, M) in CALLS:
+            xs[(name, M)].copy_(hx[(name, M)], non_blocking=True)
+            wq, sc = sets[MS.index(M) % 2][name]
+            ops.esimd_gemv_fp8_pern(xs[(name, M)], wq, sc, ys[(name, M)], N, K)
+            hy[(name, M)].copy_(ys[(name, M)], non_blocking=True)
+
+    with torch.cuda.stream(st):
+        for i in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(st)
+        for i in range(e2e_steps):
+            e2e_step()
+        a1.record(st)
+        torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(a0.elapsed_time(a1), world) / e2e_steps
+    e2e_value = STEP_BYTES * world / (e2e_ms * 1e-3) / 1e9
+
+    # --- roofline of the GEMV kernel ---
+    peak, peak_kind = peaks()
+    kern_us = sum(per_call.values())
+    achieved = STEP_BYTES / (kern_us * 1e-6) / 1e9
+    traffic = profile_traffic()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                "traffic": traffic, "algorithmic_bytes_per_step": STEP_BYTES,
+                "kernel": "cek::gemv_fp8_kernel (12 launches per step, CUDA-event timed)"}
+
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3*fp16->fp32", "data": "synthetic (seed 0: x~N(0,1) fp16, W~N(0,0.02) per-row e4m3)",
+        "config": {"workload": "BASELINE config 1: batched FP8 GEMV, per-channel fp32 scales",
+                   "shapes": {n: [N, K] for n, N, K in SHAPES}, "M": MS,
+                   "l2": "2 weight sets alternating with M: > 126 MB (L2) between two reads of one weight",
+                   "timing": "CUDA graph of the 12 launches per step, CUDA events",
+                   "parallelism": f"replicas x{world} (independent GEMV sweeps)"},
+        "us_per_call": {k: round(v, 3) for k, v in per_call.items()},
+        "roofline": roofline,
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
+                "api": "esimd_learning_b200.esimd_gemv_fp8_pern (torch op), eager"},
+        "gpu_launches": 12 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline_sample(seconds=args.cpu_seconds)
+    return out
+
+
+# ---- CPU legs (oracle port of the reference's path) -----------------------------------------
+
+def _cpu_setup():
+    torch.set_num_threads(os.cpu_count() or 1)
+    from esimd_learning_b200.workloads import make_fp8_weight
+    gen = torch.Generator().manual_seed(0)
+    ws = {name: make_fp8_weight(N, K, gen) for name, N, K in SHAPES}
+    xs = {(name, M): torch.randn(M, K, generator=gen).to(torch.float16)
+          for name, N, K in SHAPES for M in MS}
+    return ws, xs
+
+
+def _cpu_step(O, ws, xs, frac: float) -> int:
+    """Run the oracle on the first `frac` of the rows of each of the 12 GEMVs;
+    returns the algorithmic bytes processed."""
+    b = 0
+    for (name, N, K, M) in CALLS:
+        n = max(1, int(round(N * frac)))
+        wq, sc = ws[name]
+        O.gemv_fp8(xs[(name, M)], wq[:n], sc[:n])
+        b += call_bytes(M, n, K)
+    return b
+
+
+def cpu_baseline_sample(seconds: float = 15.0) -> dict:
+    from oracle import oracle as O
+    ws, xs = _cpu_setup()
+    _cpu_step(O, ws, xs, 1 / 64)  # warm
+    t0 = time.perf_counter()
+    b = _cpu_step(O, ws, xs, 1 / 16)
+    dt = time.perf_counter() - t0
+    frac = min(1.0, (1 / 16) * seconds / max(dt, 1e-3) / 2)
+    t0 = time.perf_counter()
+    b = _cpu_step(O, ws, xs, frac)
+    dt = time.perf_counter() - t0
+    return {"value": round(b / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "seconds": round(dt, 2),
+            "sample": f"first {frac:.3f} of the rows of each of the 12 config-1 GEMVs, torch fp32 "
+                      "dequant-then-matmul (the reference tests' oracle)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+    ws, xs = _cpu_setup()
+    budget = 150.0
+    _cpu_step(O, ws, xs, 1 / 256)
+    t0 = time.perf_counter()
+    _cpu_step(O, ws, xs, 1 / 64)
+    full = (time.perf_counter() - t0) * 64
+    frac = max(1 / 2048, min(1.0, budget / max(1, args.steps + args.warmup) / full))
+    for _ in range(args.warmup):
+        _cpu_step(O, ws, xs, frac)
+    t0 = time.perf_counter()
+    b = 0
+    for _ in range(args.steps):
+        b += _cpu_step(O, ws, xs, frac)
+    dt = time.perf_counter() - t0
+    value = b / dt / 1e9
+    sample = (f"each step: first {frac:.4f} of the rows of each of the 12 config-1 GEMVs "
+              "(torch fp32 dequant-then-matmul on the host cores)")
+    cores = torch.get_num_threads()
+    return {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3*fp16->fp32",
+            "data": "synthetic (seed 0)", "impl": "reference",
+            "config": {"workload": "BASELINE config 1: batched FP8 GEMV, per-channel fp32 scales",
+                       "reference_path": "oracle port of the reference tests' torch CPU oracle "
+                                         "(the reference kernels are Intel-XPU ESIMD only)"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        out = run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")))
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+    rank, world, local = dist_init(args.gpus)
+    out = run_ours(args, rank, world, local)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

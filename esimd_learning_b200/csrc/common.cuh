@@ -1,0 +1,135 @@
+// common.cuh — shared device helpers for the sm_100a FP8 custom-op kernels.
+//
+// FP8 -> 16-bit conversion.  The reference dequantises with integer bit
+// tricks and flushes FP8 subnormals to zero (csrc/xpu/esimd_kernels/
+// fp8_GEMV_v2.h:12-38).  Here every conversion is exact (subnormals kept),
+// which is what the reference tests' oracle `weight_fp8.to(torch.float16)`
+// computes (tests/test_gemv_fp8.py:31-32); both FP8 formats embed exactly in
+// fp16 and in bf16, so no rounding happens on the weight path.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/cek.h"
+
+#define CEK_DEVICE __device__ __forceinline__
+
+namespace cek {
+
+// ---- 16-byte global loads ---------------------------------------------------
+// Weights are read exactly once per call: bypass L1 so the L1/shared carve-out
+// stays with the activation tiles.
+CEK_DEVICE uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+CEK_DEVICE uint4 ldg_nc(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// ---- FP8 pair -> packed 16-bit pair -------------------------------------------
+// `pair` holds two FP8 codes in its low 16 bits (byte 0 -> low half of the
+// result, byte 1 -> high half), matching the mma.sync fragment convention that
+// the lower 16 bits carry the lower k index.
+template <int FMT>
+CEK_DEVICE uint32_t fp8x2_to_f16x2(uint32_t pair) {
+  uint32_t r;
+  if constexpr (FMT == CEK_E4M3) {
+    asm("{ .reg .b16 lo; mov.b32 {lo, _}, %1; cvt.rn.f16x2.e4m3x2 %0, lo; }"
+        : "=r"(r) : "r"(pair));
+  } else {
+    // e5m2 is the top byte of an fp16: place each byte in the high half of its lane.
+    r = __byte_perm(pair, 0u, 0x1404);
+  }
+  return r;
+}
+
+// Exact FP8 -> bf16 for a pair.  The FP8 exponent/mantissa field is placed at
+// the bottom of the bf16 exponent field, which makes the bf16 value equal to
+// the FP8 value times 2^-(127 - bias); one exact bf16x2 multiply by
+// 2^(127 - bias) restores it.  FP8 subnormals land on bf16 subnormals, which
+// the multiply handles exactly (bf16 arithmetic on sm_90+ keeps subnormals).
+template <int FMT>
+CEK_DEVICE uint32_t fp8x2_to_bf16x2(uint32_t pair) {
+  uint32_t v = __byte_perm(pair, 0u, 0x4140);  // [b0, 0, b1, 0]
+  uint32_t r;
+  if constexpr (FMT == CEK_E4M3) {
+    r = ((v & 0x007F007Fu) << 4) | ((v & 0x00800080u) << 8);
+    const uint32_t k2p120 = 0x7B807B80u;  // bf16x2 (2^120, 2^120)
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(r), "r"(k2p120));
+  } else {
+    r = ((v & 0x007F007Fu) << 5) | ((v & 0x00800080u) << 8);
+    const uint32_t k2p112 = 0x77807780u;  // bf16x2 (2^112, 2^112)
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(r), "r"(k2p112));
+  }
+  return r;
+}
+
+// ---- scalar conversions ------------------------------------------------------
+template <typename T> CEK_DEVICE float to_f32(T v);
+template <> CEK_DEVICE float to_f32<__half>(__half v) { return __half2float(v); }
+template <> CEK_DEVICE float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> CEK_DEVICE T from_f32(float v);
+template <> CEK_DEVICE __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> CEK_DEVICE __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Packed pair <-> two floats (low half first).
+template <typename T> CEK_DEVICE float2 unpack2(uint32_t u);
+template <> CEK_DEVICE float2 unpack2<__half>(uint32_t u) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  return __half22float2(h);
+}
+template <> CEK_DEVICE float2 unpack2<__nv_bfloat16>(uint32_t u) {
+  __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
+  return __bfloat1622float2(h);
+}
+template <typename T> CEK_DEVICE uint32_t pack2(float a, float b);
+template <> CEK_DEVICE uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <> CEK_DEVICE uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// ---- warp / block reductions -------------------------------------------------
+CEK_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+CEK_DEVICE float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---- programmatic dependent launch (PDL) ----------------------------------------
+// A kernel launched with cudaLaunchAttributeProgrammaticStreamSerialization may
+// start while its predecessor on the stream is still running; it must call
+// pdl_wait() before touching anything the predecessor writes.  Without the
+// attribute both instructions are no-ops.
+CEK_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+CEK_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+}  // namespace cek
+
+// Host helpers shared by the launch files.
+namespace cek_host {
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
+}
+}  // namespace cek_host

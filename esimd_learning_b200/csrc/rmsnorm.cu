@@ -1,0 +1,171 @@
+// rmsnorm.cu — residual add + RMSNorm, standalone and as the prologue of the
+// FP8 GEMV.
+//
+// Semantics follow FusedAddRmsNorm_batched_kernel
+// (csrc/xpu/esimd_kernels/fused_add_rms_norm_batched.h:22-63):
+//   pass 1  residual = fp16(hidden + residual), sum of squares over the
+//           UNROUNDED fp32 sum                                  (:32-50)
+//   pass 2  hidden = fp16(f32(residual_fp16) * inv_rms * w)      (:56-62)
+// with inv_rms = rsqrt(sum / K + eps) and w the pre-shifted (w + 1) weight.
+//
+// B200 layout: one CTA per row, 256 threads, each thread keeps its 8..64
+// elements of the row in registers between the two passes, so the row is read
+// once from HBM and written once (the reference re-reads the residual in
+// pass 2).  16-byte vector loads/stores; warp-shuffle + shared-memory
+// reduction.  Requires K % 8 == 0 and K <= 16384 (the reference requires
+// K % 512 == 0).
+#include "gemv.cuh"
+
+namespace cek {
+
+constexpr int kNormThreads = 256;
+
+template <typename T>
+CEK_DEVICE float block_sum(float v, float* sh) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x < 32) {
+    s = lane < (int)(blockDim.x >> 5) ? sh[lane] : 0.f;
+    s = warp_sum(s);
+    if (lane == 0) sh[0] = s;
+  }
+  __syncthreads();
+  return sh[0];
+}
+
+// VPT = 16-byte vectors per thread.  WRITE_NORMED: standalone op (writes the
+// normalised row into hidden).  Otherwise it is the GEMV prologue and only
+// the per-row inverse RMS is written (to inv_rms[row]).
+template <typename T, int VPT, bool WRITE_NORMED>
+__global__ void __launch_bounds__(kNormThreads)
+add_rmsnorm_kernel(T* hidden, T* residual, const T* __restrict__ weight, float* inv_rms_out,
+                   int K, float eps) {
+  __shared__ float sh[32];
+  if constexpr (!WRITE_NORMED) pdl_launch_dependents();
+  const int row = blockIdx.x;
+  const int nvec = K >> 3;
+  uint4* hrow = reinterpret_cast<uint4*>(hidden + (size_t)row * K);
+  uint4* rrow = reinterpret_cast<uint4*>(residual + (size_t)row * K);
+  uint4 rv[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + i * kNormThreads;
+    if (v < nvec) {
+      uint4 h = hrow[v], r = rrow[v];
+      uint32_t hw[4] = {h.x, h.y, h.z, h.w}, rw[4] = {r.x, r.y, r.z, r.w}, ow[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 hf = unpack2<T>(hw[q]), rf = unpack2<T>(rw[q]);
+        const float a = hf.x + rf.x, b = hf.y + rf.y;
+        ss += a * a + b * b;
+        ow[q] = pack2<T>(a, b);
+      }
+      rv[i] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      rrow[v] = rv[i];
+    }
+  }
+  const float total = block_sum<T>(ss, sh);
+  const float inv = rsqrtf(total / (float)K + eps);
+  if constexpr (!WRITE_NORMED) {
+    if (threadIdx.x == 0) inv_rms_out[row] = inv;
+  } else {
+    const uint4* wv = reinterpret_cast<const uint4*>(weight);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int v = threadIdx.x + i * kNormThreads;
+      if (v < nvec) {
+        uint4 w4 = wv[v];
+        uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+        uint32_t rw[4] = {rv[i].x, rv[i].y, rv[i].z, rv[i].w}, ow[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float2 rf = unpack2<T>(rw[q]), wf = unpack2<T>(ww[q]);
+          ow[q] = pack2<T>(rf.x * inv * wf.x, rf.y * inv * wf.y);
+        }
+        hrow[v] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      }
+    }
+  }
+}
+
+template <typename T, bool WRITE_NORMED>
+static int launch_norm(void* hidden, void* residual, const void* weight, float* inv_rms,
+                       int64_t rows, int64_t K, float eps, cudaStream_t st) {
+  const int nvec = (int)(K / 8);
+  const int vpt = (nvec + kNormThreads - 1) / kNormThreads;
+  dim3 grid((unsigned)rows), block(kNormThreads);
+  T* h = static_cast<T*>(hidden);
+  T* r = static_cast<T*>(residual);
+  const T* w = static_cast<const T*>(weight);
+#define CEK_NORM(V)                                                                              \
+  if (vpt <= V) {                                                                                \
+    add_rmsnorm_kernel<T, V, WRITE_NORMED><<<grid, block, 0, st>>>(h, r, w, inv_rms, (int)K, eps); \
+    return cek_host::launch_status();                                                            \
+  }
+  CEK_NORM(1) CEK_NORM(2) CEK_NORM(4) CEK_NORM(8)
+#undef CEK_NORM
+  return CEK_ERR_INVALID_ARG;
+}
+
+}  // namespace cek
+
+namespace {
+int check_norm_args(const void* hidden, const void* residual, int64_t rows, int64_t K, int dtype) {
+  if (rows < 0 || K <= 0 || K % 8 != 0 || K > 16384) return CEK_ERR_INVALID_ARG;
+  if (dtype != CEK_F16 && dtype != CEK_BF16) return CEK_ERR_INVALID_ARG;
+  if (rows > 0 && (!hidden || !residual)) return CEK_ERR_INVALID_ARG;
+  if (!cek_host::aligned16(hidden) || !cek_host::aligned16(residual)) return CEK_ERR_ALIGNMENT;
+  return CEK_OK;
+}
+}  // namespace
+
+extern "C" int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* weight, int64_t rows,
+                                     int64_t K, float eps, int dtype, void* stream) {
+  int s = check_norm_args(hidden, residual, rows, K, dtype);
+  if (s != CEK_OK) return s;
+  if (rows == 0) return CEK_OK;
+  if (!weight) return CEK_ERR_INVALID_ARG;
+  if (!cek_host::aligned16(weight)) return CEK_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == CEK_F16)
+    return cek::launch_norm<__half, true>(hidden, residual, weight, nullptr, rows, K, eps, st);
+  return cek::launch_norm<__nv_bfloat16, true>(hidden, residual, weight, nullptr, rows, K, eps, st);
+}
+
+extern "C" int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M) {
+  if (M < 0) return 0;
+  return ((M * (int64_t)sizeof(float) + 255) / 256) * 256;
+}
+
+extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual,
+                                              const void* norm_weight, float eps, const void* w,
+                                              const void* scale, void* y, void* workspace,
+                                              int64_t M, int64_t N, int64_t K, int dtype,
+                                              int w_fmt, int scale_kind, void* stream) {
+  int s = check_norm_args(hidden, residual, M, K, dtype);
+  if (s != CEK_OK) return s;
+  if (M > 16 || N < 0) return CEK_ERR_INVALID_ARG;
+  if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
+  if (scale_kind < CEK_SCALE_PERN_F16 || scale_kind > CEK_SCALE_PERT_F32) return CEK_ERR_INVALID_ARG;
+  if (M == 0) return CEK_OK;
+  if (!norm_weight || !w || !scale || !workspace || (N > 0 && !y)) return CEK_ERR_INVALID_ARG;
+  if (!cek_host::aligned16(norm_weight) || !cek_host::aligned16(w) || !cek_host::aligned16(workspace))
+    return CEK_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* inv = static_cast<float*>(workspace);
+  // The stats kernel only reads `hidden`; the const_cast never leads to a write.
+  void* h = const_cast<void*>(hidden);
+  s = dtype == CEK_F16
+          ? cek::launch_norm<__half, false>(h, residual, nullptr, inv, M, K, eps, st)
+          : cek::launch_norm<__nv_bfloat16, false>(h, residual, nullptr, inv, M, K, eps, st);
+  if (s != CEK_OK || N == 0) return s;
+  cek::GemvParams p = {};
+  p.x = nullptr; p.w = static_cast<const uint8_t*>(w); p.scale = scale; p.y = y;
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.residual = residual; p.gamma = norm_weight; p.inv_rms = inv;
+  return cek::gemv_launch(p, dtype, dtype, w_fmt, scale_kind, true, st);
+}

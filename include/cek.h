@@ -1,0 +1,125 @@
+/*
+ * cek.h — C ABI of the B200 (sm_100a) FP8 custom-op library `libcek_b200.so`.
+ *
+ * Every entry point takes plain device pointers, sizes and enums, enqueues its
+ * kernels on the CUDA stream passed as `stream` (a `cudaStream_t` cast to
+ * `void*`; NULL means the legacy default stream), never synchronises with the
+ * host, and returns a `cek_status` (0 = success).  No torch type crosses this
+ * boundary; the thin torch-library registration (csrc/torch_extension*.cc)
+ * turns a non-zero status into a Python RuntimeError via TORCH_CHECK.
+ *
+ * The reference (Intel ESIMD/SYCL, "custom-esimd-kernels-vllm") has no C ABI:
+ * its launch layer is a set of C++ functions taking at::Tensor.  Each entry
+ * point below names the reference function whose work it replaces, so a
+ * maintainer can map the reference's launch layer onto this library one to
+ * one.  All tensors are row-major and contiguous.
+ */
+#ifndef CEK_H_
+#define CEK_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CEK_API __attribute__((visibility("default")))
+#else
+#define CEK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+typedef enum {
+  CEK_OK = 0,
+  CEK_ERR_INVALID_ARG = 1,  /* bad size, null pointer, unknown enum value     */
+  CEK_ERR_UNSUPPORTED = 2,  /* valid arguments this build does not implement  */
+  CEK_ERR_ALIGNMENT = 3,    /* pointer or row pitch not 16-byte aligned       */
+  CEK_ERR_LAUNCH = 4,       /* cudaGetLastError() reported a launch failure   */
+  CEK_ERR_TIMEOUT = 5,      /* a bounded device-side wait ran out             */
+} cek_status;
+
+/* ---- element-type enums --------------------------------------------------- */
+typedef enum { CEK_F16 = 0, CEK_BF16 = 1 } cek_io_dtype;
+/* Same numbering as the reference's fp8_mode (esimd_kernel.sycl:14-16). */
+typedef enum { CEK_E4M3 = 0, CEK_E5M2 = 1 } cek_fp8_format;
+typedef enum {
+  CEK_SCALE_PERN_F16 = 0, /* fp16[N]: the reference's per-N scale            */
+  CEK_SCALE_PERN_F32 = 1, /* fp32[N]: per-output-channel scale               */
+  CEK_SCALE_PERT_F32 = 2, /* fp32 scalar on the device: per-tensor scale     */
+} cek_scale_kind;
+
+/* Human-readable name of a status code (static storage, never NULL). */
+CEK_API const char* cek_status_string(int status);
+
+/* Library version string, e.g. "cek_b200 0.1 sm_100a". */
+CEK_API const char* cek_version(void);
+
+/* ---- FP8-weight GEMV / small-M GEMM --------------------------------------
+ * y[m, n] = OutT( sum_k f32(x[m, k]) * f32(deq(w[n, k])) * scale(n) )
+ * x: [M, K] x_dtype; w: [N, K] fp8 (w_fmt); y: [M, N] y_dtype.
+ * scale(n) = scale[n] (per-N kinds) or scale[0] (per-tensor), read on device.
+ * Any M >= 1; K % 16 == 0; x, w, y 16-byte aligned.
+ * Replaces: GEMV_fp8_pern_host  (csrc/xpu/esimd_kernels/fp8_GEMV_v2.h:171),
+ *           GEMV_fp8_pert_host  (csrc/xpu/esimd_kernels/fp8_GEMV_v2.h:414),
+ *           GEMM_fp8_pert_dispatch, M <= 64 (csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4017). */
+CEK_API int cek_gemv_fp8(const void* x, const void* w, const void* scale, void* y,
+                 int64_t M, int64_t N, int64_t K, int x_dtype, int y_dtype,
+                 int w_fmt, int scale_kind, void* stream);
+
+/* ---- residual add + RMSNorm (batched, in place) ---------------------------
+ * residual[r, :] = fp16(hidden[r, :] + residual[r, :])
+ * hidden[r, :]   = fp16(f32(residual[r, :]) * rsqrt(mean((h + r)^2) + eps) * weight)
+ * weight is the Gemma-style pre-shifted (w + 1) vector.  rows >= 0, K % 8 == 0,
+ * K <= 16384.  Replaces: fused_add_rms_norm_batched_host
+ * (csrc/xpu/esimd_kernels/fused_add_rms_norm_batched.h:66). */
+CEK_API int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* weight,
+                          int64_t rows, int64_t K, float eps, int dtype,
+                          void* stream);
+
+/* ---- residual add + RMSNorm fused into an FP8 GEMV ------------------------
+ * residual = fp16(hidden + residual)  (in place; hidden is not written)
+ * xn       = fp16(f32(residual) * inv_rms[m] * weight)   (stays on chip)
+ * y        = GEMV(xn, w, scale)  as cek_gemv_fp8.
+ * `workspace` holds cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M) bytes of
+ * device memory (per-row inverse RMS); its contents on entry do not matter.
+ * M <= 16, K % 64 == 0, K <= 16384.  No reference counterpart: the reference
+ * runs fused_add_rms_norm_batched_host and GEMV_fp8_pern_host as two ops. */
+CEK_API int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M);
+CEK_API int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual,
+                                   const void* norm_weight, float eps,
+                                   const void* w, const void* scale, void* y,
+                                   void* workspace, int64_t M, int64_t N,
+                                   int64_t K, int dtype, int w_fmt,
+                                   int scale_kind, void* stream);
+
+/* ---- GeLU(tanh)-and-mul ----------------------------------------------------
+ * out[m, j] = gelu_tanh(x[m, j]) * x[m, d + j];  x: [M, 2d], out: [M, d].
+ * d % 8 == 0.  No reference counterpart (vLLM's gelu_tanh_and_mul layout). */
+CEK_API int cek_gelu_and_mul(const void* x, void* out, int64_t M, int64_t d, int dtype,
+                     void* stream);
+
+/* ---- per-head RMSNorm on q and k, then rotary embedding (in place) --------
+ * qkv: [M, (Hq + 2*Hkv) * D]; q heads first, then k heads, then v (untouched).
+ * q_weight, k_weight: [D] norm weights (plain multiply, not shifted).
+ * positions: int64 [M]; cos_sin_cache: fp32 [max_pos, D] with cos in the first
+ * D/2 columns and sin in the last D/2 (vLLM layout).  is_neox selects the
+ * rotate-half (1) or interleaved-pair (0) rotary convention.  D in {64,128,256}.
+ * No reference counterpart. */
+CEK_API int cek_qkv_norm_rope(void* qkv, const int64_t* positions, const void* q_weight,
+                      const void* k_weight, const float* cos_sin_cache,
+                      int64_t M, int64_t num_q_heads, int64_t num_kv_heads,
+                      int64_t head_dim, int64_t max_position, float eps,
+                      int is_neox, int dtype, void* stream);
+
+/* ---- per-token dynamic e4m3 quantisation ----------------------------------
+ * s[m] = max(amax(|a[m, :]|), 1e-12) / 448;  aq[m, k] = e4m3_rn(clamp(a / s[m])).
+ * a: [M, K] fp16/bf16; aq: [M, K] e4m3; s: fp32 [M].  K % 8 == 0.
+ * No reference counterpart (the reference GEMM takes fp16 activations). */
+CEK_API int cek_quant_fp8_per_token(const void* a, void* aq, float* a_scale, int64_t M,
+                            int64_t K, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CEK_H_ */

@@ -1,0 +1,208 @@
+"""FP8 GEMV on the GPU against the CPU oracle.
+
+Mirrors the reference's tests/test_gemv_fp8.py (shapes, data distributions,
+per-N / per-tensor / e5m2 cases, pert-vs-pern consistency) with the stricter
+max-abs <= 1e-2 * ||ref||_inf and mean-rel <= 2e-3
+(oracle.MAX_ABS_FRAC / oracle.MEAN_REL).  Every case runs through the C ABI
+(esimd_learning_b200.cabi) and through the torch op.
+"""
+import pytest
+import torch
+
+from esimd_learning_b200 import cabi
+from esimd_learning_b200.workloads import CONFIG1_MS, CONFIG1_SHAPES, gemv_case
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+# reference tests/test_gemv_fp8.py:20-21, 48, 337-338, 396
+REF_SHAPES_BASIC = [(3072, 2560), (2560, 2048), (20480, 2560), (2560, 10240),
+                    (256, 2560), (2048, 128), (3072, 2048), (16, 2048)]
+REF_SHAPES_SCALE = [(3072, 2560), (2560, 2048), (20480, 2560), (2560, 10240), (128, 2048),
+                    (2560, 10752)]
+REF_SHAPES_PERT = [(1024, 1024), (2560, 2048), (512, 2048), (3072, 2048), (128, 2048), (16, 2048),
+                   (2048, 512)]
+
+
+def cabi_gemv(x, w, scale, y, per_tensor=False):
+    M, K = x.shape
+    N = w.shape[0]
+    cabi.call("cek_gemv_fp8", cabi.ptr(x), cabi.ptr(w), cabi.ptr(scale), cabi.ptr(y), M, N, K,
+              cabi.io_dtype(x), cabi.io_dtype(y), cabi.fp8_format(w),
+              cabi.scale_kind(scale, N, per_tensor), cabi.current_stream())
+    return y
+
+
+def test_golden_vectors_through_cabi(cuda_device, golden_cases):
+    n = 0
+    for c in golden_cases:
+        if c["kind"] not in ("gemv_pern", "gemv_pert", "gemm_pert"):
+            continue
+        x = c["input"].to(cuda_device)
+        w = c["weight"].to(cuda_device)
+        s = c["scale"].to(cuda_device).reshape(-1)
+        y = torch.zeros(x.shape[0], c["N"], dtype=x.dtype, device=cuda_device)
+        cabi_gemv(x, w, s, y, per_tensor=c["kind"] != "gemv_pern")
+        torch.cuda.synchronize()
+        O.assert_parity(y, c["ref"], f"{c['kind']} N={c['N']} K={c['K']}")
+        n += 1
+    assert n >= 20
+
+
+@pytest.mark.parametrize("N,K", REF_SHAPES_BASIC)
+def test_correctness_basic(ext, cuda_device, N, K):
+    torch.manual_seed(0)
+    weight_fp8 = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(torch.float8_e4m3fn)
+    scale = torch.ones(N, dtype=torch.float16)
+    x = torch.randn(1, K, dtype=torch.float16) * 0.1
+    out = torch.zeros(1, N, dtype=torch.float16, device=cuda_device)
+    ext.esimd_gemv_fp8_pern(x.to(cuda_device), weight_fp8.to(cuda_device), scale.to(cuda_device),
+                            out, N, K)
+    O.assert_parity(out, O.gemv_fp8(x, weight_fp8, scale), f"N={N} K={K}")
+
+
+@pytest.mark.parametrize("N,K", REF_SHAPES_SCALE)
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_correctness_with_scale(ext, cuda_device, N, K, io):
+    torch.manual_seed(1)
+    weight_fp8 = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(torch.float8_e4m3fn)
+    scale = torch.randn(N, dtype=torch.float16) * 0.1
+    x = (torch.rand(1, K, dtype=torch.float16) * 0.1).to(io)
+    out = torch.zeros(1, N, dtype=io, device=cuda_device)
+    ext.esimd_gemv_fp8_pern(x.to(cuda_device), weight_fp8.to(cuda_device), scale.to(cuda_device),
+                            out, N, K)
+    O.assert_parity(out, O.gemv_fp8(x, weight_fp8, scale), f"N={N} K={K} {io}")
+
+
+@pytest.mark.parametrize("N,K", REF_SHAPES_PERT)
+def test_pert_correctness(ext, cuda_device, N, K):
+    torch.manual_seed(2)
+    weight_fp8 = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(torch.float8_e4m3fn)
+    scale_t = torch.tensor(0.05 + torch.rand(1).item() * 0.1, dtype=torch.float32)
+    x = torch.randn(1, K, dtype=torch.float16) * 0.1
+    out = torch.zeros(1, N, dtype=torch.float16, device=cuda_device)
+    ext.esimd_gemv_fp8_pert(x.to(cuda_device), weight_fp8.to(cuda_device), scale_t.to(cuda_device),
+                            out)
+    O.assert_parity(out, O.gemv_fp8(x, weight_fp8, scale_t), f"N={N} K={K}")
+
+
+@pytest.mark.parametrize("N,K", [(2560, 2048), (512, 2048), (128, 2048)])
+def test_pert_vs_pern(ext, cuda_device, N, K):
+    """reference tests/test_gemv_fp8.py:361-388 (rel < 0.01)."""
+    torch.manual_seed(3)
+    w = (torch.randn(N, K, dtype=torch.float16, device=cuda_device) * 0.1).to(torch.float8_e4m3fn)
+    x = torch.randn(1, K, dtype=torch.float16, device=cuda_device) * 0.1
+    sp = torch.full((N,), 0.073, dtype=torch.float16, device=cuda_device)
+    st = torch.tensor(0.073, dtype=torch.float32, device=cuda_device)
+    a = torch.zeros(1, N, dtype=torch.float16, device=cuda_device)
+    b = torch.zeros(1, N, dtype=torch.float16, device=cuda_device)
+    ext.esimd_gemv_fp8_pern(x, w, sp, a, N, K)
+    ext.esimd_gemv_fp8_pert(x, w, st, b)
+    rel = (a.float() - b.float()).abs().max().item() / a.float().abs().max().item()
+    assert rel < 0.01
+
+
+@pytest.mark.parametrize("N,K", [(1024, 1024), (2560, 2048), (512, 2048), (128, 2048), (16, 2048)])
+@pytest.mark.parametrize("per_tensor", [False, True])
+def test_e5m2_correctness(ext, cuda_device, N, K, per_tensor):
+    torch.manual_seed(4)
+    w = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(torch.float8_e5m2)
+    x = torch.randn(1, K, dtype=torch.float16) * 0.1
+    s = torch.tensor(0.08) if per_tensor else torch.randn(N, dtype=torch.float16) * 0.1
+    out = torch.zeros(1, N, dtype=torch.float16, device=cuda_device)
+    if per_tensor:
+        ext.esimd_gemv_fp8_pert(x.to(cuda_device), w.to(cuda_device), s.to(cuda_device), out)
+    else:
+        ext.esimd_gemv_fp8_pern(x.to(cuda_device), w.to(cuda_device), s.to(cuda_device), out, N, K)
+    O.assert_parity(out, O.gemv_fp8(x, w, s), f"e5m2 N={N} K={K}")
+
+
+def test_config0_north_star(cuda_device):
+    """x ~ N(0,1) [1,4096], W per-row e4m3 (rowabsmax/448), seed 0."""
+    x, wq, s = gemv_case(1, 4096, 4096, seed=0)
+    y = torch.zeros(1, 4096, dtype=torch.float16, device=cuda_device)
+    cabi_gemv(x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y)
+    torch.cuda.synchronize()
+    O.assert_parity(y, O.gemv_fp8(x, wq, s), "config 0")
+
+
+@pytest.mark.parametrize("name", list(CONFIG1_SHAPES))
+@pytest.mark.parametrize("M", CONFIG1_MS)
+def test_config1_batched(cuda_device, name, M):
+    """batched GEMV, M in {1,2,4,8}; down (K=14336) is the split-K case."""
+    N, K = CONFIG1_SHAPES[name]
+    x, wq, s = gemv_case(M, N, K, seed=0)
+    y = torch.zeros(M, N, dtype=torch.float16, device=cuda_device)
+    cabi_gemv(x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y)
+    torch.cuda.synchronize()
+    O.assert_parity(y, O.gemv_fp8(x, wq, s), f"config1 {name} M={M}")
+
+
+@pytest.mark.parametrize("M,N,K", [(3, 17, 16), (5, 1, 48), (16, 33, 80), (9, 200, 1040),
+                                   (17, 64, 256), (40, 100, 512), (1, 8, 4096)])
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_ragged_shapes(cuda_device, M, N, K, io):
+    """N not a multiple of the 16-row group, K not a multiple of the 64-k chunk,
+    M across token-tile boundaries, mixed fp32 [N] scale."""
+    x, wq, s = gemv_case(M, N, K, seed=M * 1000 + N, dtype=io)
+    y = torch.full((M, N), float("nan"), dtype=io, device=cuda_device)
+    cabi_gemv(x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y)
+    torch.cuda.synchronize()
+    O.assert_parity(y, O.gemv_fp8(x, wq, s), f"M={M} N={N} K={K}")
+
+
+def test_mixed_io_dtypes_cabi(cuda_device):
+    """The C ABI allows input and output dtypes to differ (the reference host
+    code instantiates all four combinations, fp8_GEMV_v2.h:181-190)."""
+    x, wq, s = gemv_case(2, 256, 1024, seed=5)
+    for xi, yo in ((torch.float16, torch.bfloat16), (torch.bfloat16, torch.float16)):
+        xx = x.to(xi)
+        y = torch.zeros(2, 256, dtype=yo, device=cuda_device)
+        cabi_gemv(xx.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y)
+        torch.cuda.synchronize()
+        O.assert_parity(y, O.gemv_fp8(xx, wq, s, out_dtype=yo), f"{xi}->{yo}")
+
+
+def test_deterministic(cuda_device):
+    x, wq, s = gemv_case(4, 4096, 14336, seed=7)
+    x, wq, s = x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device)
+    a = torch.zeros(4, 4096, dtype=torch.float16, device=cuda_device)
+    b = torch.zeros_like(a)
+    cabi_gemv(x, wq, s, a)
+    cabi_gemv(x, wq, s, b)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_reference_dtype_errors(ext, cuda_device):
+    """Reference TORCH_CHECK messages (esimd_kernel.sycl:26-37)."""
+    x = torch.zeros(1, 64, dtype=torch.float32, device=cuda_device)
+    w = torch.zeros(16, 64, dtype=torch.float8_e4m3fn, device=cuda_device)
+    s = torch.ones(16, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(RuntimeError, match="input must be fp16 or bf16"):
+        ext.esimd_gemv_fp8_pern(x, w, s, torch.zeros(1, 16, dtype=torch.float16, device=cuda_device),
+                                16, 64)
+    with pytest.raises(RuntimeError, match="same dtype"):
+        ext.esimd_gemv_fp8_pern(x.half(), w, s,
+                                torch.zeros(1, 16, dtype=torch.bfloat16, device=cuda_device), 16, 64)
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        ext.esimd_gemv_fp8_pern(torch.zeros(1, 24, dtype=torch.float16, device=cuda_device),
+                                torch.zeros(16, 24, dtype=torch.float8_e4m3fn, device=cuda_device), s,
+                                torch.zeros(1, 16, dtype=torch.float16, device=cuda_device), 16, 24)
+
+
+def test_cuda_graph_capture(ext, cuda_device):
+    """The op allocates nothing and never syncs: it captures into a CUDA graph."""
+    x, wq, s = gemv_case(1, 4096, 4096, seed=0, device=cuda_device)
+    y = torch.zeros(1, 4096, dtype=torch.float16, device=cuda_device)
+    ext.esimd_gemv_fp8_pern(x, wq, s, y, 4096, 4096)
+    ref = y.clone()
+    y.zero_()
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            ext.esimd_gemv_fp8_pern(x, wq, s, y, 4096, 4096)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)

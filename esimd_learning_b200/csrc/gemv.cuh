@@ -2,6 +2,7 @@
 // add+RMSNorm prologue variant.
 #pragma once
 #include "common.cuh"
+#include <type_traits>
 
 namespace cek {
 
@@ -19,10 +20,86 @@ struct GemvParams {
   const void* residual;   // [M, K] updated residual (written by the stats kernel)
   const void* gamma;      // [K]
   const float* inv_rms;   // [M]
+  // stream-K variant only
+  int* counters;          // [pairs] arrival counters (zero between calls)
+  float* partials;        // [pairs][max_contrib][32][8*NT] fp32 partial sums
+  int max_contrib;        // most CTAs sharing one 32-row pair
+  int uk;                 // K units per pair
+  int pairs;              // 32-row pairs
 };
 
-// Plans the split-K shape and launches the GEMV (with PDL) on `st`.
+// ---- device helpers shared by both GEMV kernels ----------------------------------
+
+template <typename InT>
+CEK_DEVICE void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+
+template <>
+CEK_DEVICE void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <>
+CEK_DEVICE void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <typename InT, int FMT>
+CEK_DEVICE uint32_t cvt_pair(uint32_t pair) {
+  if constexpr (std::is_same<InT, __half>::value) return fp8x2_to_f16x2<FMT>(pair);
+  else return fp8x2_to_bf16x2<FMT>(pair);
+}
+
+template <int SCALE>
+CEK_DEVICE float load_scale(const void* s, int n) {
+  if constexpr (SCALE == CEK_SCALE_PERN_F16) return __half2float(reinterpret_cast<const __half*>(s)[n]);
+  else if constexpr (SCALE == CEK_SCALE_PERN_F32) return reinterpret_cast<const float*>(s)[n];
+  else return reinterpret_cast<const float*>(s)[0];
+}
+
+// 16 activations of one token at k .. k+15 as 8 packed pairs.
+template <typename InT, bool FUSED>
+CEK_DEVICE void load_x16(const GemvParams& p, int tok, int k, uint32_t (&xw)[8]) {
+  if constexpr (!FUSED) {
+    const InT* xp = reinterpret_cast<const InT*>(p.x) + (size_t)tok * p.K + k;
+    uint4 a = ldg_nc(xp), b = ldg_nc(xp + 8);
+    xw[0] = a.x; xw[1] = a.y; xw[2] = a.z; xw[3] = a.w;
+    xw[4] = b.x; xw[5] = b.y; xw[6] = b.z; xw[7] = b.w;
+  } else {
+    // Residual was written by the preceding stats kernel: plain (coherent) loads.
+    const InT* rp = reinterpret_cast<const InT*>(p.residual) + (size_t)tok * p.K + k;
+    const InT* gp = reinterpret_cast<const InT*>(p.gamma) + k;
+    const uint4* rv = reinterpret_cast<const uint4*>(rp);
+    uint4 r0 = rv[0], r1 = rv[1];
+    uint4 g0 = ldg_nc(gp), g1 = ldg_nc(gp + 8);
+    const float s = p.inv_rms[tok];
+    uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    uint32_t gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float2 rf = unpack2<InT>(rr[i]);
+      float2 gf = unpack2<InT>(gg[i]);
+      xw[i] = pack2<InT>(rf.x * s * gf.x, rf.y * s * gf.y);
+    }
+  }
+}
+
+// In-CTA split-K GEMV (any M, no scratch), launched with PDL on `st`.
 int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
                 bool fused, cudaStream_t st);
+
+// Stream-K GEMV (M <= 16) and the scratch it needs (0 when not applicable).
+int64_t gemv_streamk_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int gemv_streamk_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
+                        bool fused, void* workspace, int64_t ws_bytes, cudaStream_t st);
+
+// Picks the stream-K kernel when M <= 16 and `workspace` is large enough,
+// else the in-CTA split-K kernel.
+int gemv_run(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind, bool fused,
+             void* workspace, int64_t ws_bytes, cudaStream_t st);
 
 }  // namespace cek

@@ -39,64 +39,6 @@ constexpr int kMaxWarps = 16;
 
 
 
-template <typename InT>
-CEK_DEVICE void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
-
-template <>
-CEK_DEVICE void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-template <>
-CEK_DEVICE void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-template <typename InT, int FMT>
-CEK_DEVICE uint32_t cvt_pair(uint32_t pair) {
-  if constexpr (std::is_same<InT, __half>::value) return fp8x2_to_f16x2<FMT>(pair);
-  else return fp8x2_to_bf16x2<FMT>(pair);
-}
-
-template <int SCALE>
-CEK_DEVICE float load_scale(const void* s, int n) {
-  if constexpr (SCALE == CEK_SCALE_PERN_F16) return __half2float(reinterpret_cast<const __half*>(s)[n]);
-  else if constexpr (SCALE == CEK_SCALE_PERN_F32) return reinterpret_cast<const float*>(s)[n];
-  else return reinterpret_cast<const float*>(s)[0];
-}
-
-// 16 activations of one token at k .. k+15 as 8 packed pairs.
-template <typename InT, bool FUSED>
-CEK_DEVICE void load_x16(const GemvParams& p, int tok, int k, uint32_t (&xw)[8]) {
-  if constexpr (!FUSED) {
-    const InT* xp = reinterpret_cast<const InT*>(p.x) + (size_t)tok * p.K + k;
-    uint4 a = ldg_nc(xp), b = ldg_nc(xp + 8);
-    xw[0] = a.x; xw[1] = a.y; xw[2] = a.z; xw[3] = a.w;
-    xw[4] = b.x; xw[5] = b.y; xw[6] = b.z; xw[7] = b.w;
-  } else {
-    // Residual was written by the preceding stats kernel: plain (coherent) loads.
-    const InT* rp = reinterpret_cast<const InT*>(p.residual) + (size_t)tok * p.K + k;
-    const InT* gp = reinterpret_cast<const InT*>(p.gamma) + k;
-    const uint4* rv = reinterpret_cast<const uint4*>(rp);
-    uint4 r0 = rv[0], r1 = rv[1];
-    uint4 g0 = ldg_nc(gp), g1 = ldg_nc(gp + 8);
-    const float s = p.inv_rms[tok];
-    uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-    uint32_t gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float2 rf = unpack2<InT>(rr[i]);
-      float2 gf = unpack2<InT>(gg[i]);
-      xw[i] = pack2<InT>(rf.x * s * gf.x, rf.y * s * gf.y);
-    }
-  }
-}
-
 template <typename InT, int FMT, int SCALE, typename OutT, int NT, bool FUSED>
 __global__ void __launch_bounds__(kMaxWarps * 32)
 gemv_fp8_kernel(const GemvParams p) {
@@ -265,13 +207,25 @@ int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int
   return dispatch_fmt_scale<__nv_bfloat16, __nv_bfloat16, false>(p, L, w_fmt, scale_kind, st);
 }
 
+int gemv_run(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind, bool fused,
+             void* workspace, int64_t ws_bytes, cudaStream_t st) {
+  if (workspace && base.M <= 16 && ws_bytes >= gemv_streamk_workspace_bytes(base.M, base.N, base.K))
+    return gemv_streamk_launch(base, x_dtype, y_dtype, w_fmt, scale_kind, fused, workspace, ws_bytes, st);
+  return gemv_launch(base, x_dtype, y_dtype, w_fmt, scale_kind, fused, st);
+}
+
 }  // namespace cek
+
+extern "C" int64_t cek_gemv_fp8_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  return cek::gemv_streamk_workspace_bytes(M, N, K);
+}
 
 extern "C" int cek_gemv_fp8(const void* x, const void* w, const void* scale, void* y, int64_t M,
                             int64_t N, int64_t K, int x_dtype, int y_dtype, int w_fmt,
-                            int scale_kind, void* stream) {
+                            int scale_kind, void* workspace, int64_t workspace_bytes,
+                            void* stream) {
   using namespace cek_host;
-  if (M < 0 || N < 0 || K < 0) return CEK_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0 || workspace_bytes < 0) return CEK_ERR_INVALID_ARG;
   if ((x_dtype != CEK_F16 && x_dtype != CEK_BF16) || (y_dtype != CEK_F16 && y_dtype != CEK_BF16))
     return CEK_ERR_INVALID_ARG;
   if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
@@ -279,10 +233,10 @@ extern "C" int cek_gemv_fp8(const void* x, const void* w, const void* scale, voi
   if (M == 0 || N == 0) return CEK_OK;
   if (K % 16 != 0 || N > INT32_MAX || K > INT32_MAX || M > INT32_MAX) return CEK_ERR_INVALID_ARG;
   if (!x || !w || !scale || !y) return CEK_ERR_INVALID_ARG;
-  if (!aligned16(x) || !aligned16(w)) return CEK_ERR_ALIGNMENT;
+  if (!aligned16(x) || !aligned16(w) || (workspace && !aligned16(workspace))) return CEK_ERR_ALIGNMENT;
   cek::GemvParams p = {};
   p.x = x; p.w = static_cast<const uint8_t*>(w); p.scale = scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
-  return cek::gemv_launch(p, x_dtype, y_dtype, w_fmt, scale_kind, false,
-                          static_cast<cudaStream_t>(stream));
+  return cek::gemv_run(p, x_dtype, y_dtype, w_fmt, scale_kind, false, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
 }

@@ -39,9 +39,11 @@ at::Tensor run_gemv(const char* op, at::Tensor& input, const at::Tensor& weight,
   const int fmt = fp8_format(weight, op);
   const int sk = scale_kind(scale, N, allow_per_tensor, op);
   c10::cuda::CUDAGuard guard(input.device());
+  int64_t ws_bytes = 0;
+  void* ws = workspace_for(input, cek_gemv_fp8_workspace_bytes(M, N, K), &ws_bytes);
   check_status(cek_gemv_fp8(input.data_ptr(), weight.data_ptr(), scale.data_ptr(),
                             output.data_ptr(), M, N, K, io_dtype(input), io_dtype(output), fmt,
-                            sk, stream_of(input)),
+                            sk, ws, ws_bytes, stream_of(input)),
                op);
   return output;
 }
@@ -115,11 +117,12 @@ at::Tensor esimd_fused_add_rms_norm_batched_fp8(at::Tensor hidden_states, at::Te
   const int fmt = fp8_format(qweight, op);
   const int sk = scale_kind(qweight_scale, N, true, op);
   c10::cuda::CUDAGuard guard(hidden_states.device());
-  at::Tensor ws = at::empty({cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M)},
-                            hidden_states.options().dtype(at::kByte));
+  int64_t ws_bytes = 0;
+  void* ws = workspace_for(hidden_states, cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, N, K),
+                           &ws_bytes);
   check_status(cek_fused_add_rmsnorm_gemv_fp8(
                    hidden_states.data_ptr(), residual.data_ptr(), weight.data_ptr(), (float)eps,
-                   qweight.data_ptr(), qweight_scale.data_ptr(), output.data_ptr(), ws.data_ptr(),
+                   qweight.data_ptr(), qweight_scale.data_ptr(), output.data_ptr(), ws, ws_bytes,
                    M, N, K, io_dtype(hidden_states), fmt, sk, stream_of(hidden_states)),
                op);
   return output;

@@ -32,4 +32,5 @@ from esimd_learning_b200.ops import (  # noqa: E402,F401
     esimd_gelu_and_mul,
     esimd_qkv_norm_rope,
     esimd_quant_fp8_per_token,
+    esimd_set_weight_prefetch,
 )

@@ -18,21 +18,22 @@ CEK_OK, CEK_ERR_INVALID_ARG, CEK_ERR_UNSUPPORTED, CEK_ERR_ALIGNMENT, CEK_ERR_LAU
 CEK_F16, CEK_BF16 = 0, 1
 CEK_E4M3, CEK_E5M2 = 0, 1
 CEK_SCALE_PERN_F16, CEK_SCALE_PERN_F32, CEK_SCALE_PERT_F32 = 0, 1, 2
+CEK_GEMV_EARLY_WEIGHTS = 1
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I = ctypes.c_int
 _F = ctypes.c_float
+_U = ctypes.c_uint
 
 # name -> (restype, argtypes); must list every function include/cek.h declares.
 SIGNATURES = {
     "cek_status_string": (ctypes.c_char_p, [_I]),
     "cek_version": (ctypes.c_char_p, []),
-    "cek_gemv_fp8_workspace_bytes": (_I64, [_I64, _I64, _I64]),
-    "cek_gemv_fp8": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _I, _P, _I64, _P]),
+    "cek_gemv_fp8": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _I, _U, _P]),
     "cek_fused_add_rmsnorm": (_I, [_P, _P, _P, _I64, _I64, _F, _I, _P]),
-    "cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes": (_I64, [_I64, _I64, _I64]),
-    "cek_fused_add_rmsnorm_gemv_fp8": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P]),
+    "cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes": (_I64, [_I64]),
+    "cek_fused_add_rmsnorm_gemv_fp8": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _U, _P]),
     "cek_gelu_and_mul": (_I, [_P, _P, _I64, _I64, _I, _P]),
     "cek_qkv_norm_rope": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I, _I, _P]),
     "cek_quant_fp8_per_token": (_I, [_P, _P, _P, _I64, _I64, _I, _P]),
@@ -108,18 +109,3 @@ def scale_kind(s, N: int, per_tensor: bool = False) -> int:
         return CEK_SCALE_PERN_F16
     return CEK_SCALE_PERT_F32 if (per_tensor or s.numel() == 1 and N != 1) else CEK_SCALE_PERN_F32
 
-
-_workspaces: dict = {}
-
-
-def workspace(nbytes: int, device=None):
-    """A zero-filled device workspace of at least `nbytes` (cached per device
-    and current stream; kernels leave it zero-filled after every call)."""
-    import torch
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    key = (dev.index, current_stream())
-    t = _workspaces.get(key)
-    if t is None or t.numel() < nbytes:
-        t = torch.zeros(max(nbytes, 16 << 20), dtype=torch.uint8, device=dev)
-        _workspaces[key] = t
-    return t

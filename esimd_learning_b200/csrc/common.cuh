@@ -11,6 +11,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <cstdlib>
 
 #include "../../include/cek.h"
 
@@ -128,6 +129,14 @@ CEK_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_de
 // Host helpers shared by the launch files.
 namespace cek_host {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// Programmatic dependent launch is on unless CEK_DISABLE_PDL=1 is set.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("CEK_DISABLE_PDL");
+    return !(v && v[0] == '1');
+  }();
+  return on;
+}
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;

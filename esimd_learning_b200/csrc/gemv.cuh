@@ -20,12 +20,10 @@ struct GemvParams {
   const void* residual;   // [M, K] updated residual (written by the stats kernel)
   const void* gamma;      // [K]
   const float* inv_rms;   // [M]
-  // stream-K variant only
-  int* counters;          // [pairs] arrival counters (zero between calls)
-  float* partials;        // [pairs][max_contrib][32][8*NT] fp32 partial sums
-  int max_contrib;        // most CTAs sharing one 32-row pair
-  int uk;                 // K units per pair
-  int pairs;              // 32-row pairs
+  // 1: weights may be streamed before griddepcontrol.wait (the caller
+  // guarantees the preceding kernel on the stream does not write them);
+  // 0: every global read waits for the preceding kernel.
+  int early_weights;
 };
 
 // ---- device helpers shared by both GEMV kernels ----------------------------------
@@ -91,15 +89,5 @@ CEK_DEVICE void load_x16(const GemvParams& p, int tok, int k, uint32_t (&xw)[8])
 // In-CTA split-K GEMV (any M, no scratch), launched with PDL on `st`.
 int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
                 bool fused, cudaStream_t st);
-
-// Stream-K GEMV (M <= 16) and the scratch it needs (0 when not applicable).
-int64_t gemv_streamk_workspace_bytes(int64_t M, int64_t N, int64_t K);
-int gemv_streamk_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
-                        bool fused, void* workspace, int64_t ws_bytes, cudaStream_t st);
-
-// Picks the stream-K kernel when M <= 16 and `workspace` is large enough,
-// else the in-CTA split-K kernel.
-int gemv_run(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind, bool fused,
-             void* workspace, int64_t ws_bytes, cudaStream_t st);
 
 }  // namespace cek

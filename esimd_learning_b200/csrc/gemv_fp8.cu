@@ -19,92 +19,144 @@
 //    of rows g and g+8 at k = 64c + 16t and the 16 matching activations of
 //    token g; the four 4-byte words feed four k16 MMA steps.  Any bijection
 //    of k that is the same for A and B leaves the sum unchanged.
-//  * Memory-level parallelism.  Each warp issues U = 4 chunk loads (2 x 16 B
-//    per lane each) before consuming any; with 16 warps per CTA and several
-//    CTAs per SM this keeps >40 KB per SM in flight.
+//  * Memory-level parallelism.  Each warp keeps two batches of U = 2 chunks
+//    (weights and the matching activations) in flight: the loads of batch
+//    b+1 are issued before batch b is converted and multiplied.  8-warp CTAs,
+//    ~48 warps per SM over the grid.
 //  * Split-K inside the CTA only (warps of one row group take disjoint
 //    K-slices, reduced through shared memory in a fixed order): no global
 //    scratch, no atomics, bit-reproducible results.
-//  * PDL: weights never depend on the previous kernel, so the first batch of
-//    weight loads is issued before griddepcontrol.wait; activation loads and
-//    all stores come after it.
+//  * PDL: with `early_weights` set (the preceding kernel does not write W)
+//    the first batch of weight loads is issued before griddepcontrol.wait;
+//    activation loads and all stores always come after it.
 #include "gemv.cuh"
+#include <cstdlib>
 #include <type_traits>
 
 namespace cek {
 
 constexpr int kChunkK = 64;   // k per lane-quad load round (4 lanes x 16 B)
-constexpr int kUnroll = 4;    // chunks in flight per warp
-constexpr int kMaxWarps = 16;
+constexpr int kMaxWarps = 16; // warps per CTA: max(8, ks)
 
+// Chunks per batch (two batches in flight per warp): 2 for one token tile,
+// 1 for two (their activation registers double).
+template <int NT> struct UnrollOf { static constexpr int value = NT == 1 ? 2 : 1; };
 
+// One batch: U chunks of 16 rows x 64 k of W for this warp's lanes, plus the
+// matching activations of the warp's NT token tiles.
+template <int NT>
+struct Batch {
+  static constexpr int U = UnrollOf<NT>::value;
+  uint4 wa[U], wb[U];
+  uint32_t xw[U][NT][8];
+};
+
+template <int NT>
+struct WarpCtx {
+  const uint8_t* w0;
+  const uint8_t* w1;
+  bool v0, v1;
+  int g, t, tok_base, cend;
+};
+
+template <int NT>
+CEK_DEVICE void issue_w(const GemvParams& p, const WarpCtx<NT>& c, int ch, Batch<NT>& b) {
+#pragma unroll
+  for (int u = 0; u < Batch<NT>::U; ++u) {
+    const int kk = (ch + u) * kChunkK + c.t * 16;
+    const bool ok = (ch + u < c.cend) && kk < p.K;
+    b.wa[u] = (ok && c.v0) ? ldg_stream(c.w0 + (size_t)(ch + u) * kChunkK) : make_uint4(0, 0, 0, 0);
+    b.wb[u] = (ok && c.v1) ? ldg_stream(c.w1 + (size_t)(ch + u) * kChunkK) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <typename InT, bool FUSED, int NT>
+CEK_DEVICE void issue_x(const GemvParams& p, const WarpCtx<NT>& c, int ch, Batch<NT>& b) {
+#pragma unroll
+  for (int u = 0; u < Batch<NT>::U; ++u) {
+    const int kk = (ch + u) * kChunkK + c.t * 16;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int tok = c.tok_base + j * 8 + c.g;
+      if (ch + u < c.cend && tok < p.M && kk < p.K) {
+        load_x16<InT, FUSED>(p, tok, kk, b.xw[u][j]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b.xw[u][j][i] = 0u;
+      }
+    }
+  }
+}
+
+template <typename InT, int FMT, int NT>
+CEK_DEVICE void consume(const Batch<NT>& b, float (&acc)[NT][4]) {
+#pragma unroll
+  for (int u = 0; u < Batch<NT>::U; ++u) {
+    const uint32_t wra[4] = {b.wa[u].x, b.wa[u].y, b.wa[u].z, b.wa[u].w};
+    const uint32_t wrb[4] = {b.wb[u].x, b.wb[u].y, b.wb[u].z, b.wb[u].w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint32_t a[4];
+      a[0] = cvt_pair<InT, FMT>(wra[s] & 0xFFFFu);
+      a[1] = cvt_pair<InT, FMT>(wrb[s] & 0xFFFFu);
+      a[2] = cvt_pair<InT, FMT>(wra[s] >> 16);
+      a[3] = cvt_pair<InT, FMT>(wrb[s] >> 16);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) mma16816<InT>(acc[j], a, b.xw[u][j][2 * s], b.xw[u][j][2 * s + 1]);
+    }
+  }
+}
 
 template <typename InT, int FMT, int SCALE, typename OutT, int NT, bool FUSED>
 __global__ void __launch_bounds__(kMaxWarps * 32)
 gemv_fp8_kernel(const GemvParams p) {
+  constexpr int U = Batch<NT>::U;
   __shared__ float red[kMaxWarps][16][NT * 8];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
   const int cta = blockIdx.x / p.mtiles, mt = blockIdx.x % p.mtiles;
   const int rg_local = warp / p.ks, kslice = warp % p.ks;
-  const int row0 = (cta * p.rg_per_cta + rg_local) * 16 + g;
+  WarpCtx<NT> c;
+  c.g = lane >> 2;
+  c.t = lane & 3;
+  const int row0 = (cta * p.rg_per_cta + rg_local) * 16 + c.g;
   const int row1 = row0 + 8;
-  const int tok_base = mt * NT * 8;
+  c.tok_base = mt * NT * 8;
   const int nchunks = (p.K + kChunkK - 1) / kChunkK;
   const int cbeg = kslice * p.cpw;
-  const int cend = min(cbeg + p.cpw, nchunks);
-  const bool v0 = row0 < p.N, v1 = row1 < p.N;
-  const uint8_t* w0 = p.w + (size_t)(v0 ? row0 : 0) * p.K + t * 16;
-  const uint8_t* w1 = p.w + (size_t)(v1 ? row1 : 0) * p.K + t * 16;
+  c.cend = min(cbeg + p.cpw, nchunks);
+  c.v0 = row0 < p.N;
+  c.v1 = row1 < p.N;
+  c.w0 = p.w + (size_t)(c.v0 ? row0 : 0) * p.K + c.t * 16;
+  c.w1 = p.w + (size_t)(c.v1 ? row1 : 0) * p.K + c.t * 16;
 
   float acc[NT][4];
 #pragma unroll
   for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
-  bool waited = false;
-  for (int c = cbeg; c < cend; c += kUnroll) {
-    uint4 wa[kUnroll], wb[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int kk = (c + u) * kChunkK + t * 16;
-      const bool ok = (c + u < cend) && kk < p.K;
-      wa[u] = (ok && v0) ? ldg_stream(w0 + (size_t)(c + u) * kChunkK) : make_uint4(0, 0, 0, 0);
-      wb[u] = (ok && v1) ? ldg_stream(w1 + (size_t)(c + u) * kChunkK) : make_uint4(0, 0, 0, 0);
-    }
-    if (!waited) { pdl_wait(); waited = true; }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      if (c + u >= cend) break;
-      const int kk = (c + u) * kChunkK + t * 16;
-      uint32_t xw[NT][8];
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        const int tok = tok_base + j * 8 + g;
-        if (tok < p.M && kk < p.K) {
-          load_x16<InT, FUSED>(p, tok, kk, xw[j]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) xw[j][i] = 0u;
-        }
-      }
-      const uint32_t wra[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
-      const uint32_t wrb[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        uint32_t a[4];
-        a[0] = cvt_pair<InT, FMT>(wra[s] & 0xFFFFu);
-        a[1] = cvt_pair<InT, FMT>(wrb[s] & 0xFFFFu);
-        a[2] = cvt_pair<InT, FMT>(wra[s] >> 16);
-        a[3] = cvt_pair<InT, FMT>(wrb[s] >> 16);
-#pragma unroll
-        for (int j = 0; j < NT; ++j) mma16816<InT>(acc[j], a, xw[j][2 * s], xw[j][2 * s + 1]);
-      }
-    }
+  // Two batches in flight: while one is converted and multiplied, the loads
+  // of the next are outstanding.
+  Batch<NT> A, B;
+  if (p.early_weights) {
+    issue_w(p, c, cbeg, A);
+    pdl_wait();
+  } else {
+    pdl_wait();
+    issue_w(p, c, cbeg, A);
   }
-  if (!waited) pdl_wait();
+  issue_x<InT, FUSED>(p, c, cbeg, A);
+  for (int ch = cbeg; ch < c.cend; ch += 2 * U) {
+    issue_w(p, c, ch + U, B);
+    issue_x<InT, FUSED>(p, c, ch + U, B);
+    consume<InT, FMT>(A, acc);
+    if (ch + U >= c.cend) break;
+    issue_w(p, c, ch + 2 * U, A);
+    issue_x<InT, FUSED>(p, c, ch + 2 * U, A);
+    consume<InT, FMT>(B, acc);
+  }
 
   // Cross-warp (split-K) reduction in a fixed order.
+  const int g = c.g, t = c.t;
 #pragma unroll
   for (int j = 0; j < NT; ++j) {
     red[warp][g][j * 8 + 2 * t] = acc[j][0];
@@ -117,7 +169,7 @@ gemv_fp8_kernel(const GemvParams p) {
   const int entries = rows_cta * NT * 8;
   for (int e = threadIdx.x; e < entries; e += blockDim.x) {
     const int tl = e / rows_cta, rr = e % rows_cta;
-    const int tok = tok_base + tl;
+    const int tok = c.tok_base + tl;
     const int n = cta * rows_cta + rr;
     if (tok >= p.M || n >= p.N) continue;
     const int rgl = rr >> 4, r = rr & 15;
@@ -132,17 +184,25 @@ gemv_fp8_kernel(const GemvParams p) {
 
 struct GemvLaunch { int ks, rg_per_cta, warps, cpw, mtiles, nt; int64_t ctas; };
 
-// Split-K / CTA shape heuristic.  Goal: about 32 resident warps per SM on all
-// 148 SMs with every warp owning at least one U-deep batch of chunk loads.
+// Split-K / CTA shape.  ks warps share one 16-row group (disjoint K-slices);
+// a CTA is max(8, ks) warps holding max(8, ks)/ks row groups.  ks grows
+// (up to 16) while the grid has fewer than ~48 warps per SM and every warp
+// keeps at least one pair of batches.  CEK_GEMV_KS overrides ks (tuning).
 static GemvLaunch plan_gemv(int64_t M, int64_t N, int64_t K) {
   GemvLaunch L;
   const int64_t rgs = (N + 15) / 16;
   const int64_t nchunks = (K + kChunkK - 1) / kChunkK;
-  const int64_t target_warps = 148 * 32;
+  const int64_t target_warps = 148 * 48;
   int ks = 1;
-  while (ks < 16 && rgs * ks < target_warps && nchunks >= (int64_t)(ks * 2) * kUnroll) ks *= 2;
+  const int U = M <= 8 ? UnrollOf<1>::value : UnrollOf<2>::value;
+  while (ks < kMaxWarps && rgs * ks < target_warps && nchunks >= (int64_t)(ks * 2) * 2 * U) ks *= 2;
+  static const int ks_env = [] {
+    const char* v = std::getenv("CEK_GEMV_KS");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (ks_env == 1 || ks_env == 2 || ks_env == 4 || ks_env == 8 || ks_env == 16) ks = ks_env;
   L.ks = ks;
-  L.warps = ks >= 8 ? ks : 8;
+  L.warps = ks > 8 ? ks : 8;
   L.rg_per_cta = L.warps / ks;
   L.cpw = (int)((nchunks + ks - 1) / ks);
   L.nt = M <= 8 ? 1 : 2;
@@ -160,7 +220,7 @@ static int launch_one(const GemvParams& p, const GemvLaunch& L, cudaStream_t st)
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_fp8_kernel<InT, FMT, SCALE, OutT, NT, FUSED>, p);
@@ -207,36 +267,26 @@ int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int
   return dispatch_fmt_scale<__nv_bfloat16, __nv_bfloat16, false>(p, L, w_fmt, scale_kind, st);
 }
 
-int gemv_run(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind, bool fused,
-             void* workspace, int64_t ws_bytes, cudaStream_t st) {
-  if (workspace && base.M <= 16 && ws_bytes >= gemv_streamk_workspace_bytes(base.M, base.N, base.K))
-    return gemv_streamk_launch(base, x_dtype, y_dtype, w_fmt, scale_kind, fused, workspace, ws_bytes, st);
-  return gemv_launch(base, x_dtype, y_dtype, w_fmt, scale_kind, fused, st);
-}
-
 }  // namespace cek
-
-extern "C" int64_t cek_gemv_fp8_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  return cek::gemv_streamk_workspace_bytes(M, N, K);
-}
 
 extern "C" int cek_gemv_fp8(const void* x, const void* w, const void* scale, void* y, int64_t M,
                             int64_t N, int64_t K, int x_dtype, int y_dtype, int w_fmt,
-                            int scale_kind, void* workspace, int64_t workspace_bytes,
-                            void* stream) {
+                            int scale_kind, unsigned flags, void* stream) {
   using namespace cek_host;
-  if (M < 0 || N < 0 || K < 0 || workspace_bytes < 0) return CEK_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return CEK_ERR_INVALID_ARG;
   if ((x_dtype != CEK_F16 && x_dtype != CEK_BF16) || (y_dtype != CEK_F16 && y_dtype != CEK_BF16))
     return CEK_ERR_INVALID_ARG;
   if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
   if (scale_kind < CEK_SCALE_PERN_F16 || scale_kind > CEK_SCALE_PERT_F32) return CEK_ERR_INVALID_ARG;
+  if (flags & ~(unsigned)CEK_GEMV_EARLY_WEIGHTS) return CEK_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return CEK_OK;
   if (K % 16 != 0 || N > INT32_MAX || K > INT32_MAX || M > INT32_MAX) return CEK_ERR_INVALID_ARG;
   if (!x || !w || !scale || !y) return CEK_ERR_INVALID_ARG;
-  if (!aligned16(x) || !aligned16(w) || (workspace && !aligned16(workspace))) return CEK_ERR_ALIGNMENT;
+  if (!aligned16(x) || !aligned16(w)) return CEK_ERR_ALIGNMENT;
   cek::GemvParams p = {};
   p.x = x; p.w = static_cast<const uint8_t*>(w); p.scale = scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
-  return cek::gemv_run(p, x_dtype, y_dtype, w_fmt, scale_kind, false, workspace, workspace_bytes,
-                       static_cast<cudaStream_t>(stream));
+  p.early_weights = (flags & CEK_GEMV_EARLY_WEIGHTS) ? 1 : 0;
+  return cek::gemv_launch(p, x_dtype, y_dtype, w_fmt, scale_kind, false,
+                          static_cast<cudaStream_t>(stream));
 }

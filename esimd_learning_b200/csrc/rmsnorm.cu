@@ -136,12 +136,13 @@ extern "C" int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* w
   return cek::launch_norm<__nv_bfloat16, true>(hidden, residual, weight, nullptr, rows, K, eps, st);
 }
 
-// Workspace: [inv_rms: M floats, 256-byte padded][stream-K GEMV scratch].
+// Workspace: the per-row inverse RMS written by the stats kernel and read by
+// the GEMV (M floats, padded to 256 bytes).
 static int64_t inv_rms_bytes(int64_t M) { return ((M * (int64_t)sizeof(float) + 255) / 256) * 256; }
 
-extern "C" int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+extern "C" int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M) {
   if (M <= 0 || M > 16) return 0;
-  return inv_rms_bytes(M) + cek::gemv_streamk_workspace_bytes(M, N, K);
+  return inv_rms_bytes(M);
 }
 
 extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual,
@@ -149,12 +150,13 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
                                               const void* scale, void* y, void* workspace,
                                               int64_t workspace_bytes, int64_t M, int64_t N,
                                               int64_t K, int dtype, int w_fmt, int scale_kind,
-                                              void* stream) {
+                                              unsigned flags, void* stream) {
   int s = check_norm_args(hidden, residual, M, K, dtype);
   if (s != CEK_OK) return s;
   if (M > 16 || N < 0 || workspace_bytes < 0) return CEK_ERR_INVALID_ARG;
   if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
   if (scale_kind < CEK_SCALE_PERN_F16 || scale_kind > CEK_SCALE_PERT_F32) return CEK_ERR_INVALID_ARG;
+  if (flags & ~(unsigned)CEK_GEMV_EARLY_WEIGHTS) return CEK_ERR_INVALID_ARG;
   if (M == 0) return CEK_OK;
   if (!norm_weight || !w || !scale || !workspace || (N > 0 && !y)) return CEK_ERR_INVALID_ARG;
   if (workspace_bytes < inv_rms_bytes(M)) return CEK_ERR_INVALID_ARG;
@@ -172,7 +174,8 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
   p.x = nullptr; p.w = static_cast<const uint8_t*>(w); p.scale = scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.residual = residual; p.gamma = norm_weight; p.inv_rms = inv;
-  uint8_t* sk_ws = static_cast<uint8_t*>(workspace) + inv_rms_bytes(M);
-  return cek::gemv_run(p, dtype, dtype, w_fmt, scale_kind, true, sk_ws,
-                       workspace_bytes - inv_rms_bytes(M), st);
+  // The stats kernel never writes W: the GEMV may always prefetch it.
+  p.early_weights = 1;
+  (void)flags;
+  return cek::gemv_launch(p, dtype, dtype, w_fmt, scale_kind, true, st);
 }

@@ -7,11 +7,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
-#include <ATen/ops/zeros.h>
 
-#include <map>
-#include <mutex>
-#include <utility>
+#include <atomic>
 
 #include "cek.h"
 
@@ -62,26 +59,14 @@ inline int scale_kind(const at::Tensor& s, int64_t N, bool allow_per_tensor, con
   return CEK_SCALE_PERT_F32;
 }
 
-// Zero-filled scratch for the stream-K kernels, cached per (device, stream)
-// so calls on different streams never share one.  Kernels leave it
-// zero-filled after every call, so it is zeroed only when first allocated
-// (at least 16 MiB, enough for every decode shape, so it is not regrown
-// while a CUDA graph is being captured).
-inline void* workspace_for(const at::Tensor& like, int64_t bytes, int64_t* out_bytes) {
-  static std::mutex mu;
-  static std::map<std::pair<int, cudaStream_t>, at::Tensor> cache;
-  if (bytes <= 0) {
-    *out_bytes = 0;
-    return nullptr;
-  }
-  const int dev = like.device().index();
-  const cudaStream_t st = c10::cuda::getCurrentCUDAStream(dev).stream();
-  std::lock_guard<std::mutex> lock(mu);
-  at::Tensor& t = cache[{dev, st}];
-  if (!t.defined() || t.numel() < bytes)
-    t = at::zeros({std::max<int64_t>(bytes, int64_t(16) << 20)}, like.options().dtype(at::kByte));
-  *out_bytes = t.numel();
-  return t.data_ptr();
+// Process-wide switch: let the GEMV ops stream weights before waiting for
+// the preceding kernel (CEK_GEMV_EARLY_WEIGHTS).  Off by default; turn it on
+// (esimd_set_weight_prefetch) when no kernel writes weights right before a
+// GEMV on the same stream, as in a decode step over static weights.
+inline std::atomic<bool>& weight_prefetch() {
+  static std::atomic<bool> on{false};
+  return on;
 }
+inline unsigned gemv_flags() { return weight_prefetch().load() ? CEK_GEMV_EARLY_WEIGHTS : 0u; }
 
 }  // namespace cek_torch

@@ -39,11 +39,9 @@ at::Tensor run_gemv(const char* op, at::Tensor& input, const at::Tensor& weight,
   const int fmt = fp8_format(weight, op);
   const int sk = scale_kind(scale, N, allow_per_tensor, op);
   c10::cuda::CUDAGuard guard(input.device());
-  int64_t ws_bytes = 0;
-  void* ws = workspace_for(input, cek_gemv_fp8_workspace_bytes(M, N, K), &ws_bytes);
   check_status(cek_gemv_fp8(input.data_ptr(), weight.data_ptr(), scale.data_ptr(),
                             output.data_ptr(), M, N, K, io_dtype(input), io_dtype(output), fmt,
-                            sk, ws, ws_bytes, stream_of(input)),
+                            sk, gemv_flags(), stream_of(input)),
                op);
   return output;
 }
@@ -117,13 +115,15 @@ at::Tensor esimd_fused_add_rms_norm_batched_fp8(at::Tensor hidden_states, at::Te
   const int fmt = fp8_format(qweight, op);
   const int sk = scale_kind(qweight_scale, N, true, op);
   c10::cuda::CUDAGuard guard(hidden_states.device());
-  int64_t ws_bytes = 0;
-  void* ws = workspace_for(hidden_states, cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, N, K),
-                           &ws_bytes);
+  TORCH_CHECK(M <= 16, op, ": at most 16 rows");
+  // per-row inverse RMS: a few bytes from the caching allocator (graph-safe)
+  const int64_t ws_bytes = cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M);
+  at::Tensor ws = at::empty({ws_bytes}, hidden_states.options().dtype(at::kByte));
   check_status(cek_fused_add_rmsnorm_gemv_fp8(
                    hidden_states.data_ptr(), residual.data_ptr(), weight.data_ptr(), (float)eps,
-                   qweight.data_ptr(), qweight_scale.data_ptr(), output.data_ptr(), ws, ws_bytes,
-                   M, N, K, io_dtype(hidden_states), fmt, sk, stream_of(hidden_states)),
+                   qweight.data_ptr(), qweight_scale.data_ptr(), output.data_ptr(), ws.data_ptr(),
+                   ws_bytes, M, N, K, io_dtype(hidden_states), fmt, sk, 0u,
+                   stream_of(hidden_states)),
                op);
   return output;
 }
@@ -181,6 +181,9 @@ at::Tensor esimd_qkv_norm_rope(at::Tensor qkv, at::Tensor positions, at::Tensor 
   return qkv;
 }
 
+// New: process-wide switch for CEK_GEMV_EARLY_WEIGHTS; returns the old value.
+bool esimd_set_weight_prefetch(bool enable) { return weight_prefetch().exchange(enable); }
+
 TORCH_LIBRARY(custom_esimd_kernels_vllm, m) {
   m.def("esimd_gemv_fp8_pern(Tensor input, Tensor weight, Tensor weight_scale, "
         "Tensor output, int N, int K) -> Tensor");
@@ -203,6 +206,7 @@ TORCH_LIBRARY(custom_esimd_kernels_vllm, m) {
         "Tensor cos_sin_cache, int num_q_heads, int num_kv_heads, int head_dim, float eps, "
         "bool is_neox) -> Tensor");
   m.impl("esimd_qkv_norm_rope", c10::DispatchKey::CUDA, &esimd_qkv_norm_rope);
+  m.def("esimd_set_weight_prefetch(bool enable) -> bool", &esimd_set_weight_prefetch);
 }
 
 PyMODINIT_FUNC PyInit_custom_esimd_kernels() {

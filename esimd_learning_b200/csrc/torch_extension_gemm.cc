@@ -32,11 +32,9 @@ at::Tensor esimd_gemm_fp8_pert(at::Tensor input, at::Tensor weight, at::Tensor w
   TORCH_CHECK(output.numel() == M * N, op, ": output must be [M, N]");
   const int fmt = fp8_format(weight, op);
   c10::cuda::CUDAGuard guard(input.device());
-  int64_t ws_bytes = 0;
-  void* ws = workspace_for(input, cek_gemv_fp8_workspace_bytes(M, N, K), &ws_bytes);
   check_status(cek_gemv_fp8(input.data_ptr(), weight.data_ptr(), weight_scale.data_ptr(),
                             output.data_ptr(), M, N, K, io_dtype(input), io_dtype(output), fmt,
-                            CEK_SCALE_PERT_F32, ws, ws_bytes, stream_of(input)),
+                            CEK_SCALE_PERT_F32, gemv_flags(), stream_of(input)),
                op);
   return output;
 }

@@ -109,3 +109,13 @@ def esimd_quant_fp8_per_token(
     """Dynamic per-token e4m3 quantisation: scale[m] = max(amax_m, 1e-12) / 448,
     output = e4m3(clamp(input / scale[m], -448, 448)).  Returns output."""
     return _ops.esimd_quant_fp8_per_token(input, output, scale)
+
+
+def esimd_set_weight_prefetch(enable: bool) -> bool:
+    """Let the FP8 GEMV ops start streaming weights before the preceding
+    kernel on the stream has finished (programmatic dependent launch), which
+    hides launch and DRAM latency between back-to-back decode kernels.  Only
+    valid while no kernel writes a GEMV's weights immediately before that
+    GEMV on the same stream (true for static model weights).  Process-wide;
+    returns the previous setting."""
+    return _ops.esimd_set_weight_prefetch(enable)

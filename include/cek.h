@@ -59,23 +59,21 @@ CEK_API const char* cek_version(void);
  * y[m, n] = OutT( sum_k f32(x[m, k]) * f32(deq(w[n, k])) * scale(n) )
  * x: [M, K] x_dtype; w: [N, K] fp8 (w_fmt); y: [M, N] y_dtype.
  * scale(n) = scale[n] (per-N kinds) or scale[0] (per-tensor), read on device.
- * Any M >= 1; K % 16 == 0; x, w (and workspace) 16-byte aligned.
+ * Any M >= 1; K % 16 == 0; x and w 16-byte aligned.  No scratch memory.
  *
- * workspace: device scratch for the stream-K kernel used when M <= 16.
- * Pass NULL (or fewer than cek_gemv_fp8_workspace_bytes(M, N, K) bytes) to
- * run the scratch-free in-CTA split-K kernel instead.  The workspace must be
- * zero-filled before its first use; every call leaves it zero-filled again.
- * Calls that may run concurrently (different streams) need distinct
- * workspaces.  w is read before the kernel's grid-dependency wait (PDL): it
- * must not be written by the kernel launched immediately before on `stream`.
+ * The kernel is launched with programmatic dependent launch (PDL): it may
+ * start while the previous kernel on `stream` finishes.  By default every
+ * global read waits for that kernel.  flags |= CEK_GEMV_EARLY_WEIGHTS lets
+ * the weight stream start before the wait (hiding launch and DRAM latency);
+ * the caller then guarantees that the kernel launched immediately before on
+ * `stream` does not write w.
  * Replaces: GEMV_fp8_pern_host  (csrc/xpu/esimd_kernels/fp8_GEMV_v2.h:171),
  *           GEMV_fp8_pert_host  (csrc/xpu/esimd_kernels/fp8_GEMV_v2.h:414),
  *           GEMM_fp8_pert_dispatch, M <= 64 (csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4017). */
-CEK_API int64_t cek_gemv_fp8_workspace_bytes(int64_t M, int64_t N, int64_t K);
+#define CEK_GEMV_EARLY_WEIGHTS 1u
 CEK_API int cek_gemv_fp8(const void* x, const void* w, const void* scale, void* y,
                          int64_t M, int64_t N, int64_t K, int x_dtype, int y_dtype,
-                         int w_fmt, int scale_kind, void* workspace,
-                         int64_t workspace_bytes, void* stream);
+                         int w_fmt, int scale_kind, unsigned flags, void* stream);
 
 /* ---- residual add + RMSNorm (batched, in place) ---------------------------
  * residual[r, :] = fp16(hidden[r, :] + residual[r, :])
@@ -92,19 +90,22 @@ CEK_API int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* weig
  * xn       = io(f32(residual) * inv_rms[m] * weight)   (stays on chip)
  * y        = GEMV(xn, w, scale)  as cek_gemv_fp8.
  * Two launches chained by programmatic dependent launch: a per-row stats
- * kernel (residual update, inverse RMS) and the GEMV with xn formed in its
- * operand loads.  `workspace` holds at least
- * cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, N, K) bytes, zero-filled
- * before first use (every call leaves it zero-filled again).
+ * kernel (residual update, inverse RMS into `workspace`) and the GEMV, which
+ * forms xn in its operand loads and streams w while the stats kernel runs.
+ * workspace: device scratch of at least
+ * cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M) bytes, contents ignored.
+ * flags: reserved for CEK_GEMV_EARLY_WEIGHTS (the weight stream always
+ * starts early here: the stats kernel never writes w).
  * M <= 16, K % 8 == 0, K <= 16384.  No reference counterpart: the reference
  * runs fused_add_rms_norm_batched_host and GEMV_fp8_pern_host as two ops. */
-CEK_API int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M, int64_t N, int64_t K);
+CEK_API int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M);
 CEK_API int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual,
                                            const void* norm_weight, float eps,
                                            const void* w, const void* scale, void* y,
                                            void* workspace, int64_t workspace_bytes,
                                            int64_t M, int64_t N, int64_t K, int dtype,
-                                           int w_fmt, int scale_kind, void* stream);
+                                           int w_fmt, int scale_kind, unsigned flags,
+                                           void* stream);
 
 /* ---- GeLU(tanh)-and-mul ----------------------------------------------------
  * out[m, j] = gelu_tanh(x[m, j]) * x[m, d + j];  x: [M, 2d], out: [M, d].

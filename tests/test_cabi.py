@@ -28,15 +28,15 @@ def test_status_strings_and_version():
 
 
 def _gemv(**kw):
-    a = dict(x=16, w=16, s=16, y=16, M=1, N=16, K=64, xd=0, yd=0, fmt=0, sk=0, ws=0, wsb=0)
+    a = dict(x=16, w=16, s=16, y=16, M=1, N=16, K=64, xd=0, yd=0, fmt=0, sk=0, fl=0)
     a.update(kw)
     return cabi.lib().cek_gemv_fp8(a["x"], a["w"], a["s"], a["y"], a["M"], a["N"], a["K"],
-                                   a["xd"], a["yd"], a["fmt"], a["sk"], a["ws"], a["wsb"], None)
+                                   a["xd"], a["yd"], a["fmt"], a["sk"], a["fl"], None)
 
 
 @pytest.mark.parametrize("kw", [
     dict(M=-1), dict(N=-1), dict(K=24), dict(xd=2), dict(yd=-1), dict(fmt=2), dict(sk=3),
-    dict(x=0), dict(w=0), dict(s=0), dict(y=0), dict(wsb=-1),
+    dict(x=0), dict(w=0), dict(s=0), dict(y=0), dict(fl=2),
 ])
 def test_gemv_rejects_bad_arguments(kw):
     assert _gemv(**kw) == cabi.CEK_ERR_INVALID_ARG
@@ -45,7 +45,6 @@ def test_gemv_rejects_bad_arguments(kw):
 def test_gemv_alignment_and_empty():
     assert _gemv(x=8) == cabi.CEK_ERR_ALIGNMENT
     assert _gemv(w=24) == cabi.CEK_ERR_ALIGNMENT
-    assert _gemv(ws=40, wsb=1 << 20) == cabi.CEK_ERR_ALIGNMENT
     # M == 0 or N == 0: nothing to do, no launch
     assert _gemv(M=0, x=0, y=0) == cabi.CEK_OK
     assert _gemv(N=0) == cabi.CEK_OK
@@ -57,14 +56,13 @@ def test_norm_and_helpers_reject_bad_arguments():
     assert L.cek_fused_add_rmsnorm(16, 16, 16, 1, 32768, 1e-6, 0, None) == cabi.CEK_ERR_INVALID_ARG
     assert L.cek_fused_add_rmsnorm(16, 16, 16, 0, 512, 1e-6, 0, None) == cabi.CEK_OK
     assert L.cek_fused_add_rmsnorm(8, 16, 16, 1, 512, 1e-6, 0, None) == cabi.CEK_ERR_ALIGNMENT
-    assert L.cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(3, 64, 512) >= 256
-    assert L.cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(17, 64, 512) == 0
+    assert L.cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(3) == 256
+    assert L.cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(17) == 0
     assert L.cek_fused_add_rmsnorm_gemv_fp8(16, 16, 16, 1e-6, 16, 16, 16, 16, 1 << 20, 17, 64, 512, 0,
-                                            0, 0, None) == cabi.CEK_ERR_INVALID_ARG
+                                            0, 0, 0, None) == cabi.CEK_ERR_INVALID_ARG
     # workspace smaller than the inverse-RMS block
     assert L.cek_fused_add_rmsnorm_gemv_fp8(16, 16, 16, 1e-6, 16, 16, 16, 16, 8, 2, 64, 512, 0,
-                                            0, 0, None) == cabi.CEK_ERR_INVALID_ARG
-    assert L.cek_gemv_fp8_workspace_bytes(17, 64, 512) == 0  # stream-K only for M <= 16
+                                            0, 0, 0, None) == cabi.CEK_ERR_INVALID_ARG
     assert L.cek_gelu_and_mul(16, 16, 1, 12, 0, None) == cabi.CEK_ERR_INVALID_ARG
     assert L.cek_gelu_and_mul(16, 16, 0, 16, 0, None) == cabi.CEK_OK
     assert L.cek_qkv_norm_rope(16, 16, 16, 16, 16, 1, 8, 1, 96, 64, 1e-6, 1, 0,

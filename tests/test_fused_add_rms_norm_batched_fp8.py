@@ -85,12 +85,12 @@ def test_fused_matches_unfused_composition(ext, cuda_device):
 def test_fused_through_cabi(cuda_device):
     h, r, g, wq, s = fused_norm_case(3, N=200, K=1024, seed=9, device=cuda_device)
     ref_r, ref_y = O.add_rmsnorm_gemv_fp8(h.cpu(), r.cpu(), g.cpu(), 1e-6, wq.cpu(), s.cpu())
-    nbytes = cabi.lib().cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(3, 200, 1024)
-    ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
+    nbytes = cabi.lib().cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(3)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device)
     y = torch.zeros(3, 200, dtype=torch.float16, device=cuda_device)
     cabi.call("cek_fused_add_rmsnorm_gemv_fp8", cabi.ptr(h), cabi.ptr(r), cabi.ptr(g), 1e-6,
               cabi.ptr(wq), cabi.ptr(s), cabi.ptr(y), cabi.ptr(ws), nbytes, 3, 200, 1024, cabi.CEK_F16,
-              cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, cabi.current_stream())
+              cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, 0, cabi.current_stream())
     torch.cuda.synchronize()
     assert torch.equal(r.cpu(), ref_r)
     O.assert_parity(y, ref_y, "cabi fused")

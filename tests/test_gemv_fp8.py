@@ -24,26 +24,21 @@ REF_SHAPES_PERT = [(1024, 1024), (2560, 2048), (512, 2048), (3072, 2048), (128, 
                    (2048, 512)]
 
 
-KERNELS = ["streamk", "splitk"]
+FLAGS = [0, cabi.CEK_GEMV_EARLY_WEIGHTS]
 
 
-def cabi_gemv(x, w, scale, y, per_tensor=False, kernel="streamk"):
-    """Call cek_gemv_fp8 through the C ABI.  kernel="streamk" passes a
-    workspace (stream-K kernel for M <= 16), "splitk" passes none (in-CTA
-    split-K kernel)."""
+def cabi_gemv(x, w, scale, y, per_tensor=False, flags=0):
+    """Call cek_gemv_fp8 through the C ABI."""
     M, K = x.shape
     N = w.shape[0]
-    nbytes = cabi.lib().cek_gemv_fp8_workspace_bytes(M, N, K) if kernel == "streamk" else 0
-    ws = cabi.workspace(nbytes) if nbytes else None
     cabi.call("cek_gemv_fp8", cabi.ptr(x), cabi.ptr(w), cabi.ptr(scale), cabi.ptr(y), M, N, K,
               cabi.io_dtype(x), cabi.io_dtype(y), cabi.fp8_format(w),
-              cabi.scale_kind(scale, N, per_tensor), cabi.ptr(ws), ws.numel() if ws is not None else 0,
-              cabi.current_stream())
+              cabi.scale_kind(scale, N, per_tensor), flags, cabi.current_stream())
     return y
 
 
-@pytest.mark.parametrize("kernel", KERNELS)
-def test_golden_vectors_through_cabi(cuda_device, golden_cases, kernel):
+@pytest.mark.parametrize("flags", FLAGS)
+def test_golden_vectors_through_cabi(cuda_device, golden_cases, flags):
     n = 0
     for c in golden_cases:
         if c["kind"] not in ("gemv_pern", "gemv_pert", "gemm_pert"):
@@ -52,7 +47,7 @@ def test_golden_vectors_through_cabi(cuda_device, golden_cases, kernel):
         w = c["weight"].to(cuda_device)
         s = c["scale"].to(cuda_device).reshape(-1)
         y = torch.zeros(x.shape[0], c["N"], dtype=x.dtype, device=cuda_device)
-        cabi_gemv(x, w, s, y, per_tensor=c["kind"] != "gemv_pern", kernel=kernel)
+        cabi_gemv(x, w, s, y, per_tensor=c["kind"] != "gemv_pern", flags=flags)
         torch.cuda.synchronize()
         O.assert_parity(y, c["ref"], f"{c['kind']} N={c['N']} K={c['K']}")
         n += 1
@@ -136,30 +131,30 @@ def test_config0_north_star(cuda_device):
     O.assert_parity(y, O.gemv_fp8(x, wq, s), "config 0")
 
 
-@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("flags", FLAGS)
 @pytest.mark.parametrize("name", list(CONFIG1_SHAPES))
 @pytest.mark.parametrize("M", CONFIG1_MS)
-def test_config1_batched(cuda_device, name, M, kernel):
+def test_config1_batched(cuda_device, name, M, flags):
     """batched GEMV, M in {1,2,4,8}; down (K=14336) is the split-K case."""
     N, K = CONFIG1_SHAPES[name]
     x, wq, s = gemv_case(M, N, K, seed=0)
     y = torch.zeros(M, N, dtype=torch.float16, device=cuda_device)
-    cabi_gemv(x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y, kernel=kernel)
+    cabi_gemv(x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y, flags=flags)
     torch.cuda.synchronize()
-    O.assert_parity(y, O.gemv_fp8(x, wq, s), f"config1 {name} M={M} {kernel}")
+    O.assert_parity(y, O.gemv_fp8(x, wq, s), f"config1 {name} M={M} flags={flags}")
 
 
-@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("flags", FLAGS)
 @pytest.mark.parametrize("M,N,K", [(3, 17, 16), (5, 1, 48), (16, 33, 80), (9, 200, 1040),
                                    (17, 64, 256), (40, 100, 512), (1, 8, 4096), (2, 31, 3088),
                                    (1, 5000, 16384), (8, 300, 9216), (4, 4096, 1040)])
 @pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
-def test_ragged_shapes(cuda_device, M, N, K, io, kernel):
+def test_ragged_shapes(cuda_device, M, N, K, io, flags):
     """N not a multiple of the 16-row group, K not a multiple of the 64-k chunk,
     M across token-tile boundaries, mixed fp32 [N] scale."""
     x, wq, s = gemv_case(M, N, K, seed=M * 1000 + N, dtype=io)
     y = torch.full((M, N), float("nan"), dtype=io, device=cuda_device)
-    cabi_gemv(x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y, kernel=kernel)
+    cabi_gemv(x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y, flags=flags)
     torch.cuda.synchronize()
     O.assert_parity(y, O.gemv_fp8(x, wq, s), f"M={M} N={N} K={K}")
 
@@ -176,46 +171,39 @@ def test_mixed_io_dtypes_cabi(cuda_device):
         O.assert_parity(y, O.gemv_fp8(xx, wq, s, out_dtype=yo), f"{xi}->{yo}")
 
 
-@pytest.mark.parametrize("kernel", KERNELS)
-def test_deterministic(cuda_device, kernel):
+@pytest.mark.parametrize("flags", FLAGS)
+def test_deterministic(cuda_device, flags):
     x, wq, s = gemv_case(4, 4096, 14336, seed=7)
     x, wq, s = x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device)
     a = torch.zeros(4, 4096, dtype=torch.float16, device=cuda_device)
     b = torch.zeros_like(a)
-    cabi_gemv(x, wq, s, a, kernel=kernel)
-    cabi_gemv(x, wq, s, b, kernel=kernel)
+    cabi_gemv(x, wq, s, a, flags=flags)
+    cabi_gemv(x, wq, s, b, flags=flags)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
 
 
-def test_streamk_leaves_workspace_zeroed(cuda_device):
-    """Every pair counter is reset by the CTA that finishes the pair, so a
-    workspace can be reused call after call without clearing."""
-    for (M, N, K) in [(1, 4096, 14336), (8, 28672, 4096), (3, 100, 20000), (16, 6144, 4096)]:
-        x, wq, s = gemv_case(M, N, K, seed=M, device=cuda_device)
-        nbytes = cabi.lib().cek_gemv_fp8_workspace_bytes(M, N, K)
-        ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
-        y = torch.zeros(M, N, dtype=torch.float16, device=cuda_device)
-        for _ in range(3):
-            cabi.call("cek_gemv_fp8", cabi.ptr(x), cabi.ptr(wq), cabi.ptr(s), cabi.ptr(y), M, N, K,
-                      cabi.CEK_F16, cabi.CEK_F16, cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, cabi.ptr(ws),
-                      nbytes, cabi.current_stream())
-            torch.cuda.synchronize()
-            pairs = (N + 31) // 32
-            assert int(ws[: pairs * 4].view(torch.int32).abs().sum().item()) == 0
-        O.assert_parity(y, O.gemv_fp8(x.cpu(), wq.cpu(), s.cpu()), f"M={M} N={N} K={K}")
-
-
-def test_streamk_matches_splitk(cuda_device):
-    """The two kernels sum in different orders; both are within tolerance of
-    the oracle and within fp32 rounding of each other."""
-    x, wq, s = gemv_case(8, 6144, 4096, seed=11, device=cuda_device)
-    a = torch.zeros(8, 6144, dtype=torch.float16, device=cuda_device)
-    b = torch.zeros_like(a)
-    cabi_gemv(x, wq, s, a, kernel="streamk")
-    cabi_gemv(x, wq, s, b, kernel="splitk")
-    torch.cuda.synchronize()
-    assert (a.float() - b.float()).abs().max().item() <= 2e-3 * a.float().abs().max().item()
+def test_early_weights_back_to_back(ext, cuda_device):
+    """With weight prefetch on, a chain of GEMVs where each consumes the
+    previous output (only activations depend on the preceding kernel) gives
+    the same bits as with prefetch off."""
+    dims = [4096, 1024, 2048, 4096]
+    ws = [gemv_case(2, dims[i + 1], dims[i], seed=i, device=cuda_device)[1:] for i in range(3)]
+    x0 = torch.randn(2, dims[0], device=cuda_device).half()
+    outs = []
+    for prefetch in (False, True):
+        old = ext.esimd_set_weight_prefetch(prefetch)
+        try:
+            x = x0
+            for (wq, s), n, k in zip(ws, dims[1:], dims[:-1]):
+                y = torch.empty(2, n, dtype=torch.float16, device=cuda_device)
+                ext.esimd_gemv_fp8_pern(x, wq, s, y, n, k)
+                x = y
+            outs.append(x.clone())
+        finally:
+            ext.esimd_set_weight_prefetch(old)
+    assert torch.equal(outs[0], outs[1])
+    assert torch.isfinite(outs[0].float()).all()
 
 
 def test_reference_dtype_errors(ext, cuda_device):
@@ -250,3 +238,4 @@ def test_cuda_graph_capture(ext, cuda_device):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(y, ref)
+

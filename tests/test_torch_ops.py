@@ -29,7 +29,7 @@ def test_reference_schemas_are_identical(ext):
 
 def test_new_ops_registered(ext):
     for name in ("esimd_fused_add_rms_norm_batched_fp8", "esimd_gelu_and_mul",
-                 "esimd_qkv_norm_rope", "esimd_quant_fp8_per_token"):
+                 "esimd_qkv_norm_rope", "esimd_quant_fp8_per_token", "esimd_set_weight_prefetch"):
         assert hasattr(torch.ops.custom_esimd_kernels_vllm, name)
 
 
@@ -46,3 +46,8 @@ def test_cpu_tensors_fail_loudly(ext):
     with pytest.raises(NotImplementedError):
         ext.esimd_gemv_fp8_pern(x, w, s, y, 16, 64)
 
+
+
+def test_weight_prefetch_switch(ext):
+    assert ext.esimd_set_weight_prefetch(True) is False
+    assert ext.esimd_set_weight_prefetch(False) is True

@@ -289,7 +289,7 @@ def run_ours(args, rank, world, local):
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                 "traffic": traffic, "algorithmic_bytes": STEP_BYTES,
-                "kernel": "cek::gemv_fp8_streamk_kernel (12 launches per step)"}
+                "kernel": "cek::gemv_fp8_kernel (12 launches per step; traffic = ncu DRAM bytes per step)"}
 
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
@@ -391,6 +391,21 @@ def run_reference(args, rank, world):
                     "d2h_bytes_per_step": 0}}
 
 
+def profile_steps():
+    """Two eager steps of the config-1 sweep on one weight set (201 MB of
+    weights, > L2): 24 launches of the GEMV kernel, nothing else in between."""
+    import esimd_learning_b200 as ops
+    dev = torch.device("cuda", 0)
+    sets, xs, ys = build_sets(dev, n_sets=1)
+    torch.cuda.synchronize()
+    for _ in range(2):
+        for (name, N, K, M) in CALLS:
+            wq, sc = sets[0][name]
+            ops.esimd_gemv_fp8_pern(xs[(name, M)], wq, sc, ys[(name, M)], N, K)
+    torch.cuda.synchronize()
+    print("profile steps done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -399,7 +414,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="run two eager config-1 steps (24 GEMV launches) and exit; for ncu captures")
     args = ap.parse_args()
+    if args.profile:
+        profile_steps()
+        return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":

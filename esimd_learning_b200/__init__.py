@@ -20,7 +20,7 @@ try:
 except ImportError as e:  # pragma: no cover - exercised only on an unbuilt tree
     raise ImportError(
         "esimd_learning_b200 extensions are not built; run "
-        "`python -m esimd_learning_b200.build` (needs nvcc with sm_100a support)"
+        "`python esimd_learning_b200/build.py` (needs nvcc with sm_100a support)"
     ) from e
 
 from esimd_learning_b200.ops import (  # noqa: E402,F401

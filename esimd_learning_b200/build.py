@@ -11,7 +11,7 @@ symbols (csrc/xpu/torch_extension.cc:21-24, torch_extension_gemm.cc:16-20) so
 `from <package> import custom_esimd_kernels, custom_esimd_kernels_gemm`
 works as in the reference's python/custom_esimd_kernels_vllm/__init__.py:3-4.
 
-Run: python -m esimd_learning_b200.build [--force]
+Run: python esimd_learning_b200/build.py [--force]
 """
 from __future__ import annotations
 

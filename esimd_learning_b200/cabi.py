@@ -54,7 +54,7 @@ def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
         if not LIB_PATH.exists():
-            raise OSError(f"{LIB_PATH} not built; run `python -m esimd_learning_b200.build`")
+            raise OSError(f"{LIB_PATH} not built; run `python esimd_learning_b200/build.py`")
         L = ctypes.CDLL(str(LIB_PATH))
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(L, name)

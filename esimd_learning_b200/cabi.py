@@ -14,7 +14,9 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libcek_b200.so"
 HEADER_PATH = Path(__file__).resolve().parent.parent / "include" / "cek.h"
 
-CEK_OK, CEK_ERR_INVALID_ARG, CEK_ERR_UNSUPPORTED, CEK_ERR_ALIGNMENT, CEK_ERR_LAUNCH, CEK_ERR_TIMEOUT = range(6)
+(CEK_OK, CEK_ERR_INVALID_ARG, CEK_ERR_UNSUPPORTED, CEK_ERR_ALIGNMENT, CEK_ERR_LAUNCH, CEK_ERR_TIMEOUT,
+ CEK_ERR_SCRATCH_LIMIT) = range(7)
+CEK_NOALLOC_MAX_ROWS = 16
 CEK_F16, CEK_BF16 = 0, 1
 CEK_E4M3, CEK_E5M2 = 0, 1
 CEK_SCALE_PERN_F16, CEK_SCALE_PERN_F32, CEK_SCALE_PERT_F32 = 0, 1, 2
@@ -34,6 +36,7 @@ SIGNATURES = {
     "cek_fused_add_rmsnorm": (_I, [_P, _P, _P, _I64, _I64, _F, _I, _P]),
     "cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes": (_I64, [_I64]),
     "cek_fused_add_rmsnorm_gemv_fp8": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _U, _P]),
+    "cek_fused_add_rmsnorm_gemv_fp8_noalloc": (_I, [_P, _P, _P, _F, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _U, _P]),
     "cek_gelu_and_mul": (_I, [_P, _P, _I64, _I64, _I, _P]),
     "cek_qkv_norm_rope": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I, _I, _P]),
     "cek_quant_fp8_per_token": (_I, [_P, _P, _P, _I64, _I64, _I, _P]),

@@ -9,6 +9,7 @@ extern "C" const char* cek_status_string(int status) {
     case CEK_ERR_ALIGNMENT: return "pointer or pitch not 16-byte aligned";
     case CEK_ERR_LAUNCH: return "CUDA launch failed";
     case CEK_ERR_TIMEOUT: return "bounded device wait timed out";
+    case CEK_ERR_SCRATCH_LIMIT: return "size exceeds the fixed scratch of the no-allocation entry point";
     default: return "unknown status";
   }
 }

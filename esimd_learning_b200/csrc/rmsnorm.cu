@@ -16,6 +16,8 @@
 // K % 512 == 0).
 #include "gemv.cuh"
 
+#include <mutex>
+
 namespace cek {
 
 constexpr int kNormThreads = 256;
@@ -178,4 +180,52 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
   p.early_weights = 1;
   (void)flags;
   return cek::gemv_launch(p, dtype, dtype, w_fmt, scale_kind, true, st);
+}
+
+// ---- no-allocation variant ---------------------------------------------------
+// The fused op's inverse-RMS scratch as a fixed device array, sized like the
+// op's workspace for CEK_NOALLOC_MAX_ROWS rows (256 bytes).  Host code must
+// not hand `g_noalloc_inv_rms` itself to a kernel: on the host that name is a
+// shadow variable, not device memory.  It passes the device address that
+// cudaGetSymbolAddress returns for the current device, looked up on the first
+// call on each device and cached.
+constexpr int kNoallocFloats =
+    int((CEK_NOALLOC_MAX_ROWS * sizeof(float) + 255) / 256 * 256 / sizeof(float));
+static __device__ __align__(256) float g_noalloc_inv_rms[kNoallocFloats];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[kMaxDevices] = {};
+
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CEK_ERR_LAUNCH;
+  if (dev < 0 || dev >= kMaxDevices) return CEK_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_inv_rms) != cudaSuccess || !p) return CEK_ERR_LAUNCH;
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return CEK_OK;
+}
+}  // namespace
+
+extern "C" int cek_fused_add_rmsnorm_gemv_fp8_noalloc(const void* hidden, void* residual,
+                                                      const void* norm_weight, float eps,
+                                                      const void* w, const void* scale, void* y,
+                                                      int64_t M, int64_t N, int64_t K, int dtype,
+                                                      int w_fmt, int scale_kind, unsigned flags,
+                                                      void* stream) {
+  if (M > CEK_NOALLOC_MAX_ROWS) return CEK_ERR_SCRATCH_LIMIT;
+  if (M < 0) return CEK_ERR_INVALID_ARG;
+  if (M == 0) return CEK_OK;
+  float* scratch = nullptr;
+  const int s = noalloc_scratch(&scratch);
+  if (s != CEK_OK) return s;
+  return cek_fused_add_rmsnorm_gemv_fp8(hidden, residual, norm_weight, eps, w, scale, y, scratch,
+                                        int64_t(sizeof(g_noalloc_inv_rms)), M, N, K, dtype, w_fmt,
+                                        scale_kind, flags, stream);
 }

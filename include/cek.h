@@ -37,6 +37,7 @@ typedef enum {
   CEK_ERR_ALIGNMENT = 3,    /* pointer or row pitch not 16-byte aligned       */
   CEK_ERR_LAUNCH = 4,       /* cudaGetLastError() reported a launch failure   */
   CEK_ERR_TIMEOUT = 5,      /* a bounded device-side wait ran out             */
+  CEK_ERR_SCRATCH_LIMIT = 6, /* size above the fixed scratch of a no-allocation entry point */
 } cek_status;
 
 /* ---- element-type enums --------------------------------------------------- */
@@ -106,6 +107,31 @@ CEK_API int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual,
                                            int64_t M, int64_t N, int64_t K, int dtype,
                                            int w_fmt, int scale_kind, unsigned flags,
                                            void* stream);
+
+/* ---- the same fused op, with no allocation at all -------------------------
+ * For callers that cannot allocate device memory where they call this op:
+ * code running where cudaMalloc is forbidden or unavailable (a plugin's
+ * enqueue callback inside another runtime), a process whose GPU memory is
+ * handed out by its own pool at start-up, or a serving loop that must not
+ * touch an allocator per request.  They pass inputs and outputs only.
+ *
+ * Computes exactly what cek_fused_add_rmsnorm_gemv_fp8 computes.  Its per-row
+ * inverse-RMS scratch is a fixed device array inside libcek_b200.so, sized
+ * for CEK_NOALLOC_MAX_ROWS rows (256 bytes); every GPU that loads the
+ * library holds it until the process exits.  M > CEK_NOALLOC_MAX_ROWS returns
+ * CEK_ERR_SCRATCH_LIMIT.  The array needs no clearing (each call writes every
+ * row it later reads), but all calls share it: calls that overlap on the GPU
+ * (different streams, or different host threads on one device) race.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress with that device current); make that first call
+ * before any stream capture.  No counterpart in the reference. */
+#define CEK_NOALLOC_MAX_ROWS 16
+CEK_API int cek_fused_add_rmsnorm_gemv_fp8_noalloc(const void* hidden, void* residual,
+                                                   const void* norm_weight, float eps,
+                                                   const void* w, const void* scale, void* y,
+                                                   int64_t M, int64_t N, int64_t K, int dtype,
+                                                   int w_fmt, int scale_kind, unsigned flags,
+                                                   void* stream);
 
 /* ---- GeLU(tanh)-and-mul ----------------------------------------------------
  * out[m, j] = gelu_tanh(x[m, j]) * x[m, d + j];  x: [M, 2d], out: [M, d].

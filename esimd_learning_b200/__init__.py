@@ -33,4 +33,5 @@ from esimd_learning_b200.ops import (  # noqa: E402,F401
     esimd_qkv_norm_rope,
     esimd_quant_fp8_per_token,
     esimd_set_weight_prefetch,
+    esimd_gemm_fp8_pertoken_pern,
 )

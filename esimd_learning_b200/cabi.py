@@ -40,6 +40,8 @@ SIGNATURES = {
     "cek_gelu_and_mul": (_I, [_P, _P, _I64, _I64, _I, _P]),
     "cek_qkv_norm_rope": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I, _I, _P]),
     "cek_quant_fp8_per_token": (_I, [_P, _P, _P, _I64, _I64, _I, _P]),
+    "cek_gemm_fp8_scaled": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
+    "cek_gemm_fp8_timeouts": (_I, [ctypes.POINTER(ctypes.c_uint64)]),
 }
 
 

@@ -1,0 +1,356 @@
+// gemm_fp8_tcgen05.cu — prefill FP8 x FP8 GEMM on the 5th-generation tensor
+// cores (tcgen05), per-token x per-channel scales in the epilogue.
+//
+//   y[m, n] = OutT( (sum_k deq(aq[m, k]) * deq(bq[n, k])) * a_scale[m] * b_scale[n] )
+//
+// This replaces the reference's prefill route (GEMM_fp8_pert_dispatch sends
+// M > 64 to a scalar weight-stationary kernel, csrc/xpu/esimd_kernels/
+// fp8_GEMM_pert.h:165-210, 4043-4048).
+//
+// Layout: persistent kernel, one CTA per SM, 6 warps.
+//  * warp 0 (one lane): TMA producer.  128x128-byte A boxes and 256x128-byte
+//    B boxes (128-byte swizzle) into a 4-stage shared-memory ring, completion
+//    by transaction-count mbarriers.  No multicast.
+//  * warp 1: allocates 512 TMEM columns (two 128x256 fp32 accumulators) and
+//    one lane issues tcgen05.mma kind::f8f6f4 (M=128, N=256, K=32 per
+//    instruction, 4 per stage); tcgen05.commit releases each smem stage and
+//    signals each finished accumulator.
+//  * warps 2-5: epilogue.  tcgen05.ld 32 columns at a time from their TMEM
+//    lane quadrant, scale, convert, store; then hand the accumulator back so
+//    the MMA warp can start the tile after next while this one drains.
+//  Tiles are 128 (M) x 256 (N); tile t covers m-block t % num_m and n-block
+//  t / num_m, so the CTAs in flight share B blocks through L2.
+//  Every mbarrier wait is bounded: on timeout the CTA records it in a device
+//  counter (cek_gemm_fp8_timeouts), stops, waits (bounded) for its own copies
+//  and MMAs, frees its TMEM and returns.
+#include "common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace cek {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 128;  // BK in bytes (= e4m3 elements)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 6 * 32;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+constexpr uint32_t kWaitPolls = 1u << 24;
+
+__device__ unsigned long long g_timeouts;
+
+CEK_DEVICE uint32_t saddr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+CEK_DEVICE bool try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait; false means it gave up.
+CEK_DEVICE bool wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kWaitPolls; ++i) {
+    if (try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  atomicAdd(&g_timeouts, 1ull);
+  return false;
+}
+CEK_DEVICE void bar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+CEK_DEVICE void bar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+CEK_DEVICE void bar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+CEK_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+CEK_DEVICE void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+CEK_DEVICE void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major operand, rows of 128 bytes with
+// the 128-byte swizzle, 8-row core groups 1024 bytes apart.
+CEK_DEVICE uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);        // start address
+  d |= (uint64_t)1 << 16;                         // leading byte offset (unused with swizzle)
+  d |= (uint64_t)(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                         // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                         // 128-byte swizzle
+  return d;
+}
+// Instruction descriptor: fp32 accumulate, A and B e4m3, both K-major, N=256, M=128.
+constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+
+CEK_DEVICE void mma_f8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p; }"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate) : "memory");
+}
+CEK_DEVICE void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+CEK_DEVICE void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct Params {
+  const float* a_scale;
+  const float* b_scale;
+  void* y;
+  int M, N, K;
+  int num_m, num_n;
+};
+
+template <typename OutT>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.num_m * p.num_n;
+  const int kblocks = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      bar_init(saddr(&full_bar[s]), 1);
+      bar_init(saddr(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(saddr(&acc_full[b]), 1);
+      bar_init(saddr(&acc_empty[b]), 4);
+    }
+    bar_init(saddr(&drain_bar), 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     saddr(&tmem_base_sh)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      pdl_wait();
+      int it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !abort_flag; t += gridDim.x) {
+        const int mb = t % p.num_m, nb = t / p.num_m;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait(saddr(&empty_bar[s]), ((it / STAGES) & 1) ^ 1, &abort_flag)) break;
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          const uint32_t fb = saddr(&full_bar[s]);
+          bar_expect_tx(fb, STAGE_BYTES);
+          tma_load_2d(saddr(sa), &map_a, kb * BK, mb * BM, fb);
+          tma_load_2d(saddr(sa + A_BYTES), &map_b, kb * BK, nb * BN, fb);
+        }
+      }
+      // Before leaving, make sure no copy of ours is still landing (bounded).
+      for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+        wait(saddr(&full_bar[j % STAGES]), (j / STAGES) & 1, &abort_flag);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int it = 0, local = 0;
+      for (int t = blockIdx.x; t < num_tiles && !abort_flag; t += gridDim.x, ++local) {
+        const int b = local & 1;
+        if (!wait(saddr(&acc_empty[b]), ((local >> 1) & 1) ^ 1, &abort_flag)) break;
+        fence_after();
+        const uint32_t d = tmem_base + b * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait(saddr(&full_bar[s]), (it / STAGES) & 1, &abort_flag)) { ok = false; break; }
+          fence_after();
+          const uint32_t a0 = saddr(smem + s * STAGE_BYTES), b0 = a0 + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            mma_f8(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), (kb | k) ? 1u : 0u);
+          mma_commit(saddr(&empty_bar[s]));
+        }
+        if (!ok) break;
+        mma_commit(saddr(&acc_full[b]));
+      }
+      // All MMAs of this thread finished before TMEM is released (bounded).
+      mma_commit(saddr(&drain_bar));
+      wait(saddr(&drain_bar), 0, &abort_flag);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    pdl_wait();
+    const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+    OutT* y = static_cast<OutT*>(p.y);
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles && !abort_flag; t += gridDim.x, ++local) {
+      const int b = local & 1;
+      const int mb = t % p.num_m, nb = t / p.num_m;
+      if (!wait(saddr(&acc_full[b]), (local >> 1) & 1, &abort_flag)) break;
+      fence_after();
+      const int row = mb * BM + quad * 32 + lane;
+      const bool rv = row < p.M;
+      const float as = rv ? p.a_scale[row] : 0.f;
+      OutT* yrow = y + (size_t)(rv ? row : 0) * p.N;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + b * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        const int n0 = nb * BN + c;
+        if (rv && n0 < p.N) {
+          // N % 16 == 0: the chunk holds 16 or 32 valid columns
+          const bool hi = n0 + 16 < p.N;
+          uint32_t o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = n0 + 2 * i;
+            const bool nv = i < 8 || hi;
+            const float bs0 = nv ? __ldg(p.b_scale + n) : 0.f, bs1 = nv ? __ldg(p.b_scale + n + 1) : 0.f;
+            o[i] = pack2<OutT>(__uint_as_float(r[2 * i]) * as * bs0,
+                               __uint_as_float(r[2 * i + 1]) * as * bs1);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(yrow + n0);
+          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          if (hi) {
+            dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+            dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(saddr(&acc_empty[b]));
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  fence_after();
+  __syncwarp();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+}
+
+// ---- host side ---------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename OutT>
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t st) {
+  auto kern = gemm_fp8_kernel<OutT>;
+  static unsigned attr_set = 0;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned bit = 1u << (dev & 31);
+  if (!(attr_set & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+      return CEK_ERR_LAUNCH;
+    attr_set |= bit;
+  }
+  const int tiles = p.num_m * p.num_n;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(tiles < sms ? tiles : sms));
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, p) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
+}
+
+}  // namespace gemm
+}  // namespace cek
+
+extern "C" int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* a_scale,
+                                   const float* b_scale, void* y, int64_t M, int64_t N, int64_t K,
+                                   int y_dtype, void* stream) {
+  using namespace cek::gemm;
+  if (M < 0 || N < 0 || K < 0) return CEK_ERR_INVALID_ARG;
+  if (y_dtype != CEK_F16 && y_dtype != CEK_BF16) return CEK_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return CEK_OK;
+  if (K == 0 || K % BK != 0 || N % 16 != 0) return CEK_ERR_INVALID_ARG;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return CEK_ERR_INVALID_ARG;
+  if (!aq || !bq || !a_scale || !b_scale || !y) return CEK_ERR_INVALID_ARG;
+  if (!cek_host::aligned16(aq) || !cek_host::aligned16(bq) || !cek_host::aligned16(y))
+    return CEK_ERR_ALIGNMENT;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, aq, M, K, BM) || !make_map(&mb, bq, N, K, BN)) return CEK_ERR_LAUNCH;
+  Params p;
+  p.a_scale = a_scale; p.b_scale = b_scale; p.y = y;
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.num_m = (int)((M + BM - 1) / BM);
+  p.num_n = (int)((N + BN - 1) / BN);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return y_dtype == CEK_F16 ? launch<__half>(ma, mb, p, st) : launch<__nv_bfloat16>(ma, mb, p, st);
+}
+
+extern "C" int cek_gemm_fp8_timeouts(uint64_t* count) {
+  if (!count) return CEK_ERR_INVALID_ARG;
+  unsigned long long v = 0;
+  if (cudaMemcpyFromSymbol(&v, cek::gemm::g_timeouts, sizeof(v)) != cudaSuccess) return CEK_ERR_LAUNCH;
+  *count = v;
+  return CEK_OK;
+}

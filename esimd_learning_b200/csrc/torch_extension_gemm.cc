@@ -60,6 +60,38 @@ at::Tensor esimd_quant_fp8_per_token(at::Tensor input, at::Tensor output, at::Te
   return output;
 }
 
+// New: prefill FP8 x FP8 GEMM on tcgen05 with per-token x per-channel scales.
+// input_q e4m3 [M, K] (esimd_quant_fp8_per_token), input_scale fp32 [M],
+// weight e4m3 [N, K], weight_scale fp32 [N], output fp16/bf16 [M, N].
+at::Tensor esimd_gemm_fp8_pertoken_pern(at::Tensor input_q, at::Tensor input_scale, at::Tensor weight,
+                                        at::Tensor weight_scale, at::Tensor output) {
+  const char* op = "esimd_gemm_fp8_pertoken_pern";
+  check_cuda(input_q, op, "input_q");
+  check_cuda(input_scale, op, "input_scale");
+  check_cuda(weight, op, "weight");
+  check_cuda(weight_scale, op, "weight_scale");
+  check_cuda(output, op, "output");
+  TORCH_CHECK(input_q.scalar_type() == at::ScalarType::Float8_e4m3fn &&
+                  weight.scalar_type() == at::ScalarType::Float8_e4m3fn,
+              op, ": input_q and weight must be float8_e4m3fn");
+  TORCH_CHECK(input_scale.scalar_type() == at::kFloat && weight_scale.scalar_type() == at::kFloat, op,
+              ": scales must be fp32");
+  TORCH_CHECK(is_half_or_bf16(output), op, ": output must be fp16 or bf16");
+  TORCH_CHECK(weight.dim() == 2, op, ": weight must be [N, K]");
+  const int64_t N = weight.size(0), K = weight.size(1);
+  TORCH_CHECK(input_q.size(-1) == K, op, ": input_q must be [M, K]");
+  const int64_t M = input_q.numel() / K;
+  TORCH_CHECK(input_scale.numel() == M && weight_scale.numel() == N, op,
+              ": input_scale [M], weight_scale [N]");
+  TORCH_CHECK(output.numel() == M * N, op, ": output must be [M, N]");
+  c10::cuda::CUDAGuard guard(input_q.device());
+  check_status(cek_gemm_fp8_scaled(input_q.data_ptr(), weight.data_ptr(), input_scale.data_ptr<float>(),
+                                   weight_scale.data_ptr<float>(), output.data_ptr(), M, N, K,
+                                   io_dtype(output), stream_of(input_q)),
+               op);
+  return output;
+}
+
 TORCH_LIBRARY_FRAGMENT(custom_esimd_kernels_vllm, m) {
   // FP8 GEMM per-tensor scale: input [M, K] fp16, weight [N, K] fp8, output [M, N] fp16
   m.def("esimd_gemm_fp8_pert(Tensor input, Tensor weight, Tensor weight_scale, "
@@ -68,6 +100,10 @@ TORCH_LIBRARY_FRAGMENT(custom_esimd_kernels_vllm, m) {
 
   m.def("esimd_quant_fp8_per_token(Tensor input, Tensor output, Tensor scale) -> Tensor");
   m.impl("esimd_quant_fp8_per_token", c10::DispatchKey::CUDA, &esimd_quant_fp8_per_token);
+
+  m.def("esimd_gemm_fp8_pertoken_pern(Tensor input_q, Tensor input_scale, Tensor weight, "
+        "Tensor weight_scale, Tensor output) -> Tensor");
+  m.impl("esimd_gemm_fp8_pertoken_pern", c10::DispatchKey::CUDA, &esimd_gemm_fp8_pertoken_pern);
 }
 
 PyMODINIT_FUNC PyInit_custom_esimd_kernels_gemm() {

@@ -119,3 +119,16 @@ def esimd_set_weight_prefetch(enable: bool) -> bool:
     GEMV on the same stream (true for static model weights).  Process-wide;
     returns the previous setting."""
     return _ops.esimd_set_weight_prefetch(enable)
+
+
+def esimd_gemm_fp8_pertoken_pern(
+    input_q: torch.Tensor, input_scale: torch.Tensor, weight: torch.Tensor,
+    weight_scale: torch.Tensor, output: torch.Tensor,
+) -> torch.Tensor:
+    """Prefill FP8 GEMM on the Blackwell tensor cores (tcgen05):
+    output = (deq(input_q) @ deq(weight)^T) * input_scale[:, None] * weight_scale[None, :].
+
+    input_q e4m3 [M, K] with input_scale fp32 [M] (from esimd_quant_fp8_per_token),
+    weight e4m3 [N, K] with weight_scale fp32 [N], output fp16/bf16 [M, N].
+    K % 128 == 0, N % 16 == 0.  Returns output."""
+    return _ops.esimd_gemm_fp8_pertoken_pern(input_q, input_scale, weight, weight_scale, output)

@@ -159,6 +159,23 @@ CEK_API int cek_qkv_norm_rope(void* qkv, const int64_t* positions, const void* q
 CEK_API int cek_quant_fp8_per_token(const void* a, void* aq, float* a_scale, int64_t M,
                             int64_t K, int dtype, void* stream);
 
+/* ---- FP8 x FP8 GEMM, per-token x per-channel scales (tcgen05) -------------
+ * y[m, n] = OutT( (sum_k deq(aq[m, k]) * deq(bq[n, k])) * a_scale[m] * b_scale[n] )
+ * aq: [M, K] e4m3 (e.g. from cek_quant_fp8_per_token); bq: [N, K] e4m3;
+ * a_scale fp32 [M]; b_scale fp32 [N]; y: [M, N] y_dtype.
+ * K % 128 == 0, N % 16 == 0, any M; aq, bq, y 16-byte aligned.  Persistent
+ * tcgen05 kernel (TMA, TMEM accumulators); scratch-free.
+ * Replaces the prefill (M > 64) route of GEMM_fp8_pert_dispatch
+ * (csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4043-4048, the scalar
+ * weight-stationary kernel), for activations quantised per token. */
+CEK_API int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* a_scale,
+                                const float* b_scale, void* y, int64_t M, int64_t N,
+                                int64_t K, int y_dtype, void* stream);
+
+/* Number of bounded device waits in cek_gemm_fp8_scaled kernels that gave up
+ * since the library was loaded (0 in a healthy run).  Synchronous. */
+CEK_API int cek_gemm_fp8_timeouts(uint64_t* count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -309,9 +309,70 @@ def run_ours(args, rank, world, local):
         "gpu_launches": len(CALLS) * args.steps,
         "clocks": clk.summary(),
     }
+    if not args.no_gemm:
+        out["gemm"] = {f"M{M}": measure_gemm(dev, M) for M in (2048, 8192)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_sample(seconds=args.cpu_seconds)
     return out
+
+
+def fp8_peak_tflops() -> tuple[float, str]:
+    """Dense FP8 denominator: 2x the measured cuBLAS bf16 burst rate (the
+    tensor cores run e4m3 at twice the bf16 rate); fallback 2 x 1590."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return 2.0 * float(json.loads(p.read_text())["bf16_tflops"]), "2x measured bf16 burst"
+    except Exception:
+        return 2.0 * 1590.0, "2x fallback bf16"
+
+
+def measure_gemm(dev, M: int, reps: int = 20) -> dict:
+    """per-token quantisation of A [M, 4096] fp16 and the
+    tcgen05 FP8 GEMM against B [14336, 4096] e4m3 (per-channel scales).  Each
+    timed launch follows an L2 flush (256 MB write); CUDA events on the
+    launching stream; median over `reps`.  torch._scaled_mm (cuBLASLt FP8,
+    row-wise scales) on the same operands is reported beside it."""
+    import esimd_learning_b200 as ops
+    from esimd_learning_b200.workloads import prefill_case
+    N, K = 14336, 4096
+    a, bq, bs = prefill_case(M, N=N, K=K, seed=0, device=dev)
+    aq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=dev)
+    as_ = torch.empty(M, dtype=torch.float32, device=dev)
+    y = torch.empty(M, N, dtype=torch.float16, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        ts = []
+        for r in range(reps + 3):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            if r >= 3:
+                ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
+    quant_us = timed(lambda: ops.esimd_quant_fp8_per_token(a, aq, as_))
+    gemm_us = timed(lambda: ops.esimd_gemm_fp8_pertoken_pern(aq, as_, bq, bs, y))
+    flops = 2.0 * M * N * K
+    peak, src = fp8_peak_tflops()
+    tf = flops / (gemm_us * 1e-6) / 1e12
+    res = {"gemm_us": round(gemm_us, 2), "tflops": round(tf, 1), "peak_tflops": peak, "peak_source": src,
+           "frac": round(tf / peak, 4), "quant_us": round(quant_us, 2),
+           "quant_gbs": round((2 * M * K + M * K + 4 * M) / (quant_us * 1e-6) / 1e9, 1),
+           "shape": [M, N, K], "out": "fp16"}
+    try:
+        sa, sb = as_.reshape(M, 1), bs.reshape(1, N)
+        lib_us = timed(lambda: torch._scaled_mm(aq, bq.t(), scale_a=sa, scale_b=sb, out_dtype=torch.float16))
+        res["cublaslt_scaled_mm_us"] = round(lib_us, 2)
+        res["cublaslt_tflops"] = round(flops / (lib_us * 1e-6) / 1e12, 1)
+    except Exception as e:  # library path unavailable: report why
+        res["cublaslt_scaled_mm"] = f"unavailable: {type(e).__name__}"
+    del flush
+    return res
 
 
 # ---- CPU legs (oracle port of the reference's path) -----------------------------------------
@@ -414,6 +475,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
     ap.add_argument("--profile", action="store_true",
                     help="run two eager config-1 steps (24 GEMV launches) and exit; for ncu captures")
     args = ap.parse_args()

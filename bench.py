@@ -142,6 +142,7 @@ def dist_init(n_gpus: int):
         raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch with torch.distributed.run")
     if world > 1:
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     return rank, world, local
@@ -311,9 +312,73 @@ def run_ours(args, rank, world, local):
     }
     if not args.no_gemm:
         out["gemm"] = {f"M{M}": measure_gemm(dev, M) for M in (2048, 8192)}
+    if not args.no_chain:
+        out["chain"] = measure_chain(dev, rank, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_sample(seconds=args.cpu_seconds)
     return out
+
+
+def measure_chain(dev, rank: int, world: int, Ms=(1, 8), reps: int = 200) -> dict:
+    """the 70B-shaped decode step (esimd_learning_b200.chain)
+    tensor-parallel over the `world` ranks of this run (NCCL all-reduce of the
+    down projection).  L layers with distinct weights are captured in one CUDA
+    graph so that each replay streams more than 3x L2 of weights per rank;
+    time = max over ranks of the CUDA-event time per layer-step."""
+    import esimd_learning_b200 as ops
+    from esimd_learning_b200.chain import ChainShape, DecodeChain, full_weights, shard_weights
+
+    shape = ChainShape()
+    per_rank = shape.weight_bytes() // world
+    layers = max(1, -(-(3 * 126 * 2**20) // per_rank))
+    old = ops.esimd_set_weight_prefetch(True)
+    chains = {M: [] for M in Ms}
+    for l in range(layers):
+        full = full_weights(shape, seed=100 + l, device=dev)
+        sh = shard_weights(full, shape, rank, world)
+        del full
+        for M in Ms:
+            chains[M].append(DecodeChain(sh, shape, M, dev, group=None, world=world))
+        del sh
+        torch.cuda.empty_cache()
+    res = {"tp": world, "layers_per_replay": layers, "weight_bytes_per_rank_per_step": per_rank}
+    peak, _ = peaks()
+    for M in Ms:
+        g = torch.Generator(device=dev).manual_seed(7)
+        h = torch.randn(M, shape.hidden, device=dev, generator=g).half()
+        r = torch.randn(M, shape.hidden, device=dev, generator=g).half()
+        a = torch.randn(M, shape.hidden, device=dev, generator=g).half()
+        pos = torch.randint(0, shape.max_position, (M,), device=dev, generator=g)
+        st = torch.cuda.Stream(dev)
+        with torch.cuda.stream(st):
+            for c in chains[M]:
+                c.step(h, r, a, pos)  # warm-up outside capture (NCCL, modules)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=st):
+                for c in chains[M]:
+                    c.step(h, r, a, pos)
+            for _ in range(5):
+                graph.replay()
+            torch.cuda.synchronize()
+            barrier(world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+        barrier(world)
+        us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (reps * layers), world)
+        gbs = per_rank / (us * 1e-6) / 1e9
+        res[f"M{M}"] = {"us_per_step": round(us, 2), "weight_gbs_per_gpu": round(gbs, 1),
+                        "frac_of_hbm": round(gbs / peak, 4),
+                        "kernels_per_step": 7, "nccl_all_reduce": world > 1}
+        del graph
+    ops.esimd_set_weight_prefetch(old)
+    del chains
+    torch.cuda.empty_cache()
+    return res
 
 
 def fp8_peak_tflops() -> tuple[float, str]:
@@ -467,7 +532,17 @@ def profile_steps():
     print("profile steps done")
 
 
+def _claim_stdout():
+    """Route everything libraries print (NCCL banners, warnings) to stderr and
+    return a file on the real stdout for the one JSON result line."""
+    sys.stdout.flush()
+    real = os.dup(1)
+    os.dup2(2, 1)
+    return os.fdopen(real, "w")
+
+
 def main():
+    out_file = _claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8000)
@@ -476,6 +551,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
+    ap.add_argument("--no-chain", action="store_true", help="skip the config-4 decode-chain measurement")
     ap.add_argument("--profile", action="store_true",
                     help="run two eager config-1 steps (24 GEMV launches) and exit; for ncu captures")
     args = ap.parse_args()
@@ -488,12 +564,12 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         out = run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")))
         if out is not None:
-            print(json.dumps(out), flush=True)
+            print(json.dumps(out), file=out_file, flush=True)
         return
     rank, world, local = dist_init(args.gpus)
     out = run_ours(args, rank, world, local)
     if rank == 0:
-        print(json.dumps(out), flush=True)
+        print(json.dumps(out), file=out_file, flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

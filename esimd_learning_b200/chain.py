@@ -1,0 +1,168 @@
+"""Tensor-parallel decode step of a 70B-shaped layer built from the custom ops
+hidden 8192, 64 q / 8 kv heads of 128, MLP 28672.
+
+One step, on every rank (rank r of TP):
+
+1. ``esimd_fused_add_rms_norm_batched_fp8``: residual += hidden; RMSNorm
+   (replicated, every rank holds the full hidden row); the QKV GEMV over this
+   rank's heads (column-parallel, 10240 / TP output rows laid out as
+   [q heads | k heads | v heads] of the shard).
+2. ``esimd_qkv_norm_rope`` on the local heads (per-head RMSNorm of q and k,
+   RoPE theta 500000 at the token positions).  Attention itself is outside
+   this path.
+3. ``esimd_fused_add_rms_norm_batched_fp8`` again for the MLP block: residual
+   += attention output (given as an input), RMSNorm, the gate_up GEMV over
+   this rank's [gate | up] rows (column-parallel, 57344 / TP rows).
+4. ``esimd_gelu_and_mul`` on the local half-width (28672 / TP).
+5. The down GEMV on this rank's K-slice of the down weight (row-parallel,
+   K = 28672 / TP) with the full per-channel scale: a partial sum of the
+   output.
+6. NCCL all-reduce (sum) of the fp16 [M, 8192] partials; at TP = 1 it is
+   skipped.
+
+All weights are e4m3 with per-output-channel fp32 scales computed on the
+full (unsharded) matrix, so the sharded step equals the unsharded one up to
+the order of the final fp16 sums.  The step is a sequence of kernels on one
+stream with no host synchronisation, so it captures in one CUDA graph
+(``DecodeChain.capture``).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class ChainShape:
+    hidden: int = 8192
+    num_q_heads: int = 64
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    intermediate: int = 28672
+    rope_theta: float = 500000.0
+    max_position: int = 8192
+    eps: float = 1e-6
+
+    @property
+    def qkv_rows(self) -> int:
+        return (self.num_q_heads + 2 * self.num_kv_heads) * self.head_dim
+
+    def weight_bytes(self) -> int:
+        """FP8 weight bytes of one full (unsharded) step."""
+        h = self.hidden
+        return self.qkv_rows * h + 2 * self.intermediate * h + h * self.intermediate
+
+
+SMALL = ChainShape(hidden=1024, num_q_heads=8, num_kv_heads=2, head_dim=128, intermediate=2048,
+                   max_position=512)
+
+
+def _quantize_rows(w: torch.Tensor):
+    """Per-output-row e4m3 quantisation: scale = rowabsmax / 448 (fp32)."""
+    wf = w.float()
+    s = wf.abs().amax(dim=1).clamp(min=1e-12) / 448.0
+    return (wf / s[:, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn), s
+
+
+def full_weights(shape: ChainShape, seed: int = 0, device="cpu"):
+    """The unsharded weights of one layer: dict of (e4m3 [N, K], fp32 [N]) plus
+    the norm weights (gamma = 1 + 0.1 N(0,1) in fp16)."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    h, f = shape.hidden, shape.intermediate
+
+    def w(n, k):
+        return _quantize_rows(torch.randn(n, k, generator=gen, device=device) * 0.02)
+
+    out = {"qkv": w(shape.qkv_rows, h), "gate_up": w(2 * f, h), "down": w(h, f)}
+    out["gamma_attn"] = (1 + 0.1 * torch.randn(h, generator=gen, device=device)).half()
+    out["gamma_mlp"] = (1 + 0.1 * torch.randn(h, generator=gen, device=device)).half()
+    out["q_norm"] = (1 + 0.1 * torch.randn(shape.head_dim, generator=gen, device=device)).half()
+    out["k_norm"] = (1 + 0.1 * torch.randn(shape.head_dim, generator=gen, device=device)).half()
+    return out
+
+
+def shard_weights(full: dict, shape: ChainShape, rank: int, world: int) -> dict:
+    """This rank's shards.  QKV by heads (q heads, then k heads, then v heads
+    of the shard), gate_up by matching gate/up rows, down by K columns."""
+    hq, hkv, d, f = shape.num_q_heads, shape.num_kv_heads, shape.head_dim, shape.intermediate
+    if hq % world or hkv % world or f % world:
+        raise ValueError(f"TP={world} must divide q heads {hq}, kv heads {hkv} and intermediate {f}")
+    lq, lkv, lf = hq // world, hkv // world, f // world
+    wq, sq = full["qkv"]
+    qrows = torch.arange(rank * lq * d, (rank + 1) * lq * d)
+    krows = hq * d + torch.arange(rank * lkv * d, (rank + 1) * lkv * d)
+    vrows = (hq + hkv) * d + torch.arange(rank * lkv * d, (rank + 1) * lkv * d)
+    rows = torch.cat([qrows, krows, vrows]).to(wq.device)
+    wgu, sgu = full["gate_up"]
+    gu_rows = torch.cat([torch.arange(rank * lf, (rank + 1) * lf),
+                         f + torch.arange(rank * lf, (rank + 1) * lf)]).to(wgu.device)
+    wd, sd = full["down"]
+    return {
+        "qkv": (wq.view(torch.uint8)[rows].contiguous().view(torch.float8_e4m3fn), sq[rows].contiguous()),
+        "gate_up": (wgu.view(torch.uint8)[gu_rows].contiguous().view(torch.float8_e4m3fn),
+                    sgu[gu_rows].contiguous()),
+        "down": (wd.view(torch.uint8)[:, rank * lf:(rank + 1) * lf].contiguous().view(torch.float8_e4m3fn),
+                 sd.contiguous()),
+        "gamma_attn": full["gamma_attn"], "gamma_mlp": full["gamma_mlp"],
+        "q_norm": full["q_norm"], "k_norm": full["k_norm"],
+        "local_q_heads": lq, "local_kv_heads": lkv, "local_intermediate": lf,
+    }
+
+
+def rope_cache(shape: ChainShape, device) -> torch.Tensor:
+    """fp32 [max_position, head_dim] cos | sin (vLLM layout)."""
+    d = shape.head_dim
+    inv = 1.0 / (shape.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    t = torch.arange(shape.max_position, dtype=torch.float32)
+    fr = torch.outer(t, inv)
+    return torch.cat([fr.cos(), fr.sin()], dim=-1).to(device)
+
+
+class DecodeChain:
+    """One rank's executor of the decode step (module docstring).  `group`
+    is the torch.distributed process group of the TP ranks (None at TP=1)."""
+
+    def __init__(self, shards: dict, shape: ChainShape, M: int, device, group=None, world: int = 1):
+        import esimd_learning_b200 as ops
+
+        self.ops, self.shape, self.M, self.dev, self.group, self.world = ops, shape, M, device, group, world
+        self.w = {k: (tuple(t.to(device) for t in v) if isinstance(v, tuple) else
+                      (v.to(device) if torch.is_tensor(v) else v)) for k, v in shards.items()}
+        lq, lkv, lf = shards["local_q_heads"], shards["local_kv_heads"], shards["local_intermediate"]
+        d, h = shape.head_dim, shape.hidden
+        self.lq, self.lkv, self.lf = lq, lkv, lf
+        self.cos_sin = rope_cache(shape, device)
+        f16 = dict(dtype=torch.float16, device=device)
+        self.qkv = torch.empty(M, (lq + 2 * lkv) * d, **f16)
+        self.gu = torch.empty(M, 2 * lf, **f16)
+        self.act = torch.empty(M, lf, **f16)
+        self.out = torch.empty(M, h, **f16)
+        self.graph = None
+
+    def step(self, hidden, residual, attn_out, positions):
+        """Runs the step on the current stream; returns (out [M, hidden] fp16,
+        qkv [M, local qkv] fp16 after norm+RoPE).  residual is updated in place."""
+        o, s, w = self.ops, self.shape, self.w
+        o.esimd_fused_add_rms_norm_batched_fp8(hidden, residual, w["gamma_attn"], s.eps, *w["qkv"], self.qkv)
+        o.esimd_qkv_norm_rope(self.qkv, positions, w["q_norm"], w["k_norm"], self.cos_sin, self.lq, self.lkv,
+                              s.head_dim, s.eps, True)
+        o.esimd_fused_add_rms_norm_batched_fp8(attn_out, residual, w["gamma_mlp"], s.eps, *w["gate_up"],
+                                               self.gu)
+        o.esimd_gelu_and_mul(self.gu, self.act)
+        wd, sd = w["down"]
+        o.esimd_gemv_fp8_pern(self.act, wd, sd, self.out, s.hidden, self.lf)
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.out, group=self.group)
+        return self.out, self.qkv
+
+    def capture(self, hidden, residual, attn_out, positions, stream=None):
+        """Capture one step into a CUDA graph over these (static) input tensors."""
+        st = stream or torch.cuda.Stream(self.dev)
+        with torch.cuda.stream(st):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                self.step(hidden, residual, attn_out, positions)
+        self.graph = g
+        return g

@@ -224,3 +224,20 @@ def assert_parity(out: torch.Tensor, ref: torch.Tensor, what: str = "") -> dict:
     assert m["max_abs_frac"] <= MAX_ABS_FRAC, f"{what}: max-abs {m}"
     assert m["mean_rel"] <= MEAN_REL, f"{what}: mean-rel {m}"
     return m
+
+
+# ---- tensor-parallel decode step, unsharded -------------------------
+
+def decode_chain(full: dict, shape, hidden, residual, attn_out, positions):
+    """One decode step of the 70B-shaped layer on the unsharded weights:
+    add+RMSNorm -> QKV GEMV -> q/k-norm + RoPE; add+RMSNorm -> gate_up GEMV ->
+    GeLU-and-mul -> down GEMV.  Returns (out, qkv, new_residual); the sharded
+    GPU step must match it (out after the all-reduce, qkv per rank shard)."""
+    r1, qkv = add_rmsnorm_gemv_fp8(hidden, residual, full["gamma_attn"], shape.eps, *full["qkv"])
+    cs = rope_cos_sin_cache(shape.max_position, shape.head_dim, shape.rope_theta)
+    qkv = qkv_norm_rope(qkv, positions, full["q_norm"], full["k_norm"], cs, shape.num_q_heads,
+                        shape.num_kv_heads, shape.head_dim, shape.eps, True)
+    r2, gu = add_rmsnorm_gemv_fp8(attn_out, r1, full["gamma_mlp"], shape.eps, *full["gate_up"])
+    act = gelu_and_mul(gu)
+    out = gemv_fp8(act, *full["down"])
+    return out, qkv, r2

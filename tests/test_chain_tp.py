@@ -1,0 +1,128 @@
+"""Tensor-parallel decode step.
+
+CPU (no GPU): the sharding of esimd_learning_b200.chain, run as two gloo ranks
+on the oracle, must reproduce the unsharded oracle step (head-sharded QKV,
+column-parallel gate_up, row-parallel down + all-reduce).
+GPU: the DecodeChain executor at TP=1 (eager and CUDA-graph replay) against
+the oracle on a small layer.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from esimd_learning_b200.chain import SMALL, DecodeChain, full_weights, shard_weights
+from oracle import oracle as O
+
+
+def _inputs(shape, M, seed=1, device="cpu"):
+    g = torch.Generator().manual_seed(seed)
+    h = torch.randn(M, shape.hidden, generator=g).half()
+    r = torch.randn(M, shape.hidden, generator=g).half()
+    a = torch.randn(M, shape.hidden, generator=g).half()
+    pos = torch.randint(0, shape.max_position, (M,), generator=g)
+    return [t.to(device) for t in (h, r, a, pos)]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    shape, M = SMALL, 3
+    full = full_weights(shape, seed=0)
+    sh = shard_weights(full, shape, rank, world)
+    h, r, a, pos = _inputs(shape, M)
+    # the per-rank step, computed with the oracle's pieces on this rank's shards
+    r1, qkv = O.add_rmsnorm_gemv_fp8(h, r, sh["gamma_attn"], shape.eps, *sh["qkv"])
+    cs = O.rope_cos_sin_cache(shape.max_position, shape.head_dim, shape.rope_theta)
+    qkv = O.qkv_norm_rope(qkv, pos, sh["q_norm"], sh["k_norm"], cs, sh["local_q_heads"],
+                          sh["local_kv_heads"], shape.head_dim, shape.eps, True)
+    r2, gu = O.add_rmsnorm_gemv_fp8(a, r1, sh["gamma_mlp"], shape.eps, *sh["gate_up"])
+    act = O.gelu_and_mul(gu)
+    part = O.gemv_fp8(act, *sh["down"], out_dtype=torch.float32)
+    dist.all_reduce(part)
+    q.put((rank, part.half(), qkv, r2))
+    dist.destroy_process_group()
+
+
+def test_tp2_sharding_matches_unsharded_oracle():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, out, qkv, r2 = q.get(timeout=300)
+        res[rank] = (out, qkv, r2)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    shape = SMALL
+    full = full_weights(shape, seed=0)
+    h, r, a, pos = _inputs(shape, 3)
+    out, qkv, r2 = O.decode_chain(full, shape, h, r, a, pos)
+    d, lq, lkv = shape.head_dim, shape.num_q_heads // world, shape.num_kv_heads // world
+    for rank in range(world):
+        o_r, qkv_r, r2_r = res[rank]
+        O.assert_parity(o_r, out, f"rank {rank} out")
+        assert torch.equal(r2_r, r2)
+        q_full = qkv[:, : shape.num_q_heads * d].reshape(3, -1, d)[:, rank * lq:(rank + 1) * lq]
+        k_full = qkv[:, shape.num_q_heads * d:(shape.num_q_heads + shape.num_kv_heads) * d]
+        k_full = k_full.reshape(3, -1, d)[:, rank * lkv:(rank + 1) * lkv]
+        got = qkv_r.reshape(3, -1, d)
+        torch.testing.assert_close(got[:, :lq].float(), q_full.float(), rtol=0, atol=0)
+        torch.testing.assert_close(got[:, lq:lq + lkv].float(), k_full.float(), rtol=0, atol=0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_chain_tp1_gpu_vs_oracle(ext, cuda_device, M):
+    shape = SMALL
+    full = full_weights(shape, seed=0)
+    chain = DecodeChain(shard_weights(full, shape, 0, 1), shape, M, cuda_device)
+    h, r, a, pos = _inputs(shape, M, seed=M)
+    ref_out, ref_qkv, ref_r = O.decode_chain(full, shape, h, r, a, pos)
+    hd, rd, ad, pd = (t.to(cuda_device) for t in (h, r, a, pos))
+    out, qkv = chain.step(hd, rd, ad, pd)
+    torch.cuda.synchronize()
+    assert torch.equal(rd.cpu(), ref_r)
+    O.assert_parity(qkv, ref_qkv, "qkv")
+    O.assert_parity(out, ref_out, "out")
+    # graph replay of the same step from the same starting residual
+    rd.copy_(r.to(cuda_device))
+    chain.capture(hd, rd, ad, pd)
+    rd.copy_(r.to(cuda_device))
+    out.zero_()
+    chain.graph.replay()
+    torch.cuda.synchronize()
+    O.assert_parity(out, ref_out, "graph out")
+
+
+@pytest.mark.gpu
+def test_chain_tp_nccl_gpu():
+    """TP=2 on two GPUs with NCCL (skipped on a one-GPU box)."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs two GPUs")
+    worker = Path(__file__).resolve().parent / "chain_tp_worker.py"
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(worker)],
+                       capture_output=True, text=True, timeout=600,
+                       env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]

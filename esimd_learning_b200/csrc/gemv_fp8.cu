@@ -130,6 +130,12 @@ gemv_fp8_kernel(const GemvParams p) {
   c.w0 = p.w + (size_t)(c.v0 ? row0 : 0) * p.K + c.t * 16;
   c.w1 = p.w + (size_t)(c.v1 ? row1 : 0) * p.K + c.t * 16;
 
+  // Every CTA of this grid is resident once each has passed this point: let
+  // the next kernel on the stream launch into the slots the tail frees.  It
+  // waits (griddepcontrol.wait) for this grid's completion before reading
+  // anything this grid writes.
+  pdl_launch_dependents();
+
   float acc[NT][4];
 #pragma unroll
   for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -203,6 +209,11 @@ static GemvLaunch plan_gemv(int64_t M, int64_t N, int64_t K) {
   if (ks_env == 1 || ks_env == 2 || ks_env == 4 || ks_env == 8 || ks_env == 16) ks = ks_env;
   L.ks = ks;
   L.warps = ks > 8 ? ks : 8;
+  static const int warps_env = [] {
+    const char* v = std::getenv("CEK_GEMV_WARPS");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (warps_env == 8 || warps_env == 16) L.warps = warps_env > ks ? warps_env : ks;
   L.rg_per_cta = L.warps / ks;
   L.cpw = (int)((nchunks + ks - 1) / ks);
   L.nt = M <= 8 ? 1 : 2;

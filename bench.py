@@ -557,6 +557,23 @@ def _claim_stdout():
     return os.fdopen(real, "w")
 
 
+def profile_gemm(M: int):
+    """Two launches each of the per-token quantisation and the tcgen05 GEMM of
+    BASELINE config 3 at this M (A [M, 4096], B [14336, 4096])."""
+    import esimd_learning_b200 as ops
+    from esimd_learning_b200.workloads import prefill_case
+    dev = torch.device("cuda", 0)
+    a, bq, bs = prefill_case(M, device=dev)
+    aq = torch.empty(M, 4096, dtype=torch.float8_e4m3fn, device=dev)
+    as_ = torch.empty(M, dtype=torch.float32, device=dev)
+    y = torch.empty(M, 14336, dtype=torch.float16, device=dev)
+    for _ in range(2):
+        ops.esimd_quant_fp8_per_token(a, aq, as_)
+        ops.esimd_gemm_fp8_pertoken_pern(aq, as_, bq, bs, y)
+    torch.cuda.synchronize()
+    print("profile gemm done")
+
+
 def main():
     out_file = _claim_stdout()
     ap = argparse.ArgumentParser()
@@ -569,11 +586,16 @@ def main():
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
     ap.add_argument("--no-chain", action="store_true", help="skip the config-4 decode-chain measurement")
     ap.add_argument("--no-prefetch", action="store_true", help="GEMVs wait for the previous kernel before any load")
+    ap.add_argument("--profile-gemm", type=int, default=0, metavar="M",
+                    help="run quant + tcgen05 GEMM of config 3 at this M twice and exit; for ncu")
     ap.add_argument("--profile", action="store_true",
                     help="run two eager config-1 steps (24 GEMV launches) and exit; for ncu captures")
     args = ap.parse_args()
     if args.profile:
         profile_steps()
+        return
+    if args.profile_gemm:
+        profile_gemm(args.profile_gemm)
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -28,17 +28,27 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 namespace cek {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 128;  // BK in bytes (= e4m3 elements)
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int BM = 128, BK = 128;  // BK in bytes (= e4m3 elements)
 constexpr int THREADS = 6 * 32;
-constexpr int TMEM_COLS = 2 * BN;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+constexpr int TMEM_COLS = 512;     // two accumulators of up to 256 fp32 columns
+constexpr int kSmemBudget = 227 * 1024;
+
+// Tile-N dependent constants.  BN is a multiple of 32 in [128, 256]; the
+// stage count fills the shared-memory budget.
+template <int BN>
+struct Tile {
+  static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (kSmemBudget - 2048) / STAGE_BYTES > 6 ? 6 : (kSmemBudget - 2048) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  // fp32 accumulate, A and B e4m3, both K-major, N = BN, M = 128
+  static constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+};
 constexpr uint32_t kWaitPolls = 1u << 24;
 
 __device__ unsigned long long g_timeouts;
@@ -90,14 +100,11 @@ CEK_DEVICE uint64_t smem_desc(uint32_t addr) {
   d |= (uint64_t)2 << 61;                         // 128-byte swizzle
   return d;
 }
-// Instruction descriptor: fp32 accumulate, A and B e4m3, both K-major, N=256, M=128.
-constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
-
-CEK_DEVICE void mma_f8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+CEK_DEVICE void mma_f8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p; }"
-      ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate) : "memory");
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
 }
 CEK_DEVICE void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -125,10 +132,11 @@ struct Params {
   int num_m, num_n;
 };
 
-template <typename OutT>
+template <typename OutT, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const Params p) {
+  constexpr int STAGES = Tile<BN>::STAGES, STAGE_BYTES = Tile<BN>::STAGE_BYTES, A_BYTES = Tile<BN>::A_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
@@ -193,7 +201,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         const int b = local & 1;
         if (!wait(saddr(&acc_empty[b]), ((local >> 1) & 1) ^ 1, &abort_flag)) break;
         fence_after();
-        const uint32_t d = tmem_base + b * BN;
+        const uint32_t d = tmem_base + b * 256;
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES;
@@ -202,7 +210,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           const uint32_t a0 = saddr(smem + s * STAGE_BYTES), b0 = a0 + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k)
-            mma_f8(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), (kb | k) ? 1u : 0u);
+            mma_f8(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), Tile<BN>::IDESC, (kb | k) ? 1u : 0u);
           mma_commit(saddr(&empty_bar[s]));
         }
         if (!ok) break;
@@ -227,7 +235,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       const bool rv = row < p.M;
       const float as = rv ? p.a_scale[row] : 0.f;
       OutT* yrow = y + (size_t)(rv ? row : 0) * p.N;
-      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + b * BN;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + b * 256;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -283,6 +291,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  // box_rows <= 256 (TMA box limit); BN and BM are both within it
   auto enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -294,9 +303,10 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename OutT>
+template <typename OutT, int BN>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t st) {
-  auto kern = gemm_fp8_kernel<OutT>;
+  auto kern = gemm_fp8_kernel<OutT, BN>;
+  constexpr int SMEM_BYTES = Tile<BN>::SMEM_BYTES;
   static unsigned attr_set = 0;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -336,15 +346,41 @@ extern "C" int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* 
   if (!aq || !bq || !a_scale || !b_scale || !y) return CEK_ERR_INVALID_ARG;
   if (!cek_host::aligned16(aq) || !cek_host::aligned16(bq) || !cek_host::aligned16(y))
     return CEK_ERR_ALIGNMENT;
+  // Tile N: the candidate that minimises (rounds of tiles over the SMs) x BN,
+  // i.e. the persistent grid's critical path.  A narrower tile must win by
+  // more than 3 %: per FLOP it is slightly slower (measured: at M = 8192,
+  // N = 14336 BN = 256 beats 224 although its cost is 2 % higher).
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t num_m = (M + BM - 1) / BM;
+  const int cands[4] = {256, 224, 192, 160};
+  int bn = 256;
+  int64_t best = INT64_MAX / 100;
+  for (int c : cands) {
+    const int64_t tiles = num_m * ((N + c - 1) / c);
+    const int64_t cost = ((tiles + sms - 1) / sms) * c;
+    if (cost * 100 < best * 97) { best = cost; bn = c; }
+  }
+  static const int bn_env = [] {  // CEK_GEMM_BN forces the tile N (tuning only)
+    const char* v = std::getenv("CEK_GEMM_BN");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (bn_env == 256 || bn_env == 224 || bn_env == 192 || bn_env == 160) bn = bn_env;
   CUtensorMap ma, mb;
-  if (!make_map(&ma, aq, M, K, BM) || !make_map(&mb, bq, N, K, BN)) return CEK_ERR_LAUNCH;
+  if (!make_map(&ma, aq, M, K, BM) || !make_map(&mb, bq, N, K, bn)) return CEK_ERR_LAUNCH;
   Params p;
   p.a_scale = a_scale; p.b_scale = b_scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
-  p.num_m = (int)((M + BM - 1) / BM);
-  p.num_n = (int)((N + BN - 1) / BN);
+  p.num_m = (int)num_m;
+  p.num_n = (int)((N + bn - 1) / bn);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return y_dtype == CEK_F16 ? launch<__half>(ma, mb, p, st) : launch<__nv_bfloat16>(ma, mb, p, st);
+#define CEK_GEMM_BN(B)                                                                        \
+  if (bn == B) return y_dtype == CEK_F16 ? launch<__half, B>(ma, mb, p, st)                  \
+                                         : launch<__nv_bfloat16, B>(ma, mb, p, st);
+  CEK_GEMM_BN(256) CEK_GEMM_BN(224) CEK_GEMM_BN(192) CEK_GEMM_BN(160)
+#undef CEK_GEMM_BN
+  return CEK_ERR_UNSUPPORTED;
 }
 
 extern "C" int cek_gemm_fp8_timeouts(uint64_t* count) {

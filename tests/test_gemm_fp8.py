@@ -58,7 +58,7 @@ def _prefill(ext, dev, M, N, K, io=torch.float16, seed=0):
     return y, O.gemm_fp8_scaled(aq, as_, bq, bs, out_dtype=io)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (256, 512, 512), (100, 272, 256), (300, 1040, 384),
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (256, 512, 512), (100, 272, 256), (300, 1040, 384), (640, 2240, 256), (130, 3840, 128),
                                    (1, 16, 128), (129, 4096, 1024)])
 @pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
 def test_tcgen05_gemm_small(ext, cuda_device, M, N, K, io):

@@ -102,7 +102,10 @@ qkv_norm_rope_kernel(T* qkv, const int64_t* __restrict__ pos, const T* __restric
 
 // ---- per-token dynamic e4m3 quantisation -------------------------------------
 // s = max(amax, 1e-12) / 448 with IEEE division; q = e4m3_rn_sat(a / s).
-template <typename T>
+// One CTA per row, 256 threads; the row stays in registers between the amax
+// reduction and the quantisation (VPT 16-byte vectors per thread, K <= 16384),
+// so it is read from HBM once.
+template <typename T, int VPT>
 __global__ void __launch_bounds__(256)
 quant_fp8_per_token_kernel(const T* __restrict__ a, uint8_t* __restrict__ q, float* __restrict__ sc,
                            int K) {
@@ -110,13 +113,16 @@ quant_fp8_per_token_kernel(const T* __restrict__ a, uint8_t* __restrict__ q, flo
   const int m = blockIdx.x;
   const T* row = a + (size_t)m * K;
   const int nvec = K >> 3;
+  uint4 v[VPT];
   float amax = 0.f;
-  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-    const uint4 u = *reinterpret_cast<const uint4*>(row + v * 8);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = unpack2<T>(w[i]);
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * 256;
+    v[i] = idx < nvec ? *reinterpret_cast<const uint4*>(row + idx * 8) : make_uint4(0, 0, 0, 0);
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack2<T>(w[j]);
       amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
     }
   }
@@ -124,27 +130,29 @@ quant_fp8_per_token_kernel(const T* __restrict__ a, uint8_t* __restrict__ q, flo
   if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = amax;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
-    v = warp_max(v);
-    if (threadIdx.x == 0) sh[0] = v;
+    float t = threadIdx.x < 8 ? sh[threadIdx.x] : 0.f;
+    t = warp_max(t);
+    if (threadIdx.x == 0) sh[0] = t;
   }
   __syncthreads();
   const float s = __fdiv_rn(fmaxf(sh[0], 1e-12f), 448.f);
   if (threadIdx.x == 0) sc[m] = s;
-  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-    const uint4 u = *reinterpret_cast<const uint4*>(row + v * 8);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int idx = threadIdx.x + i * 256;
+    if (idx >= nvec) continue;
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
     uint32_t packed[2] = {0u, 0u};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = unpack2<T>(w[i]);
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack2<T>(w[j]);
       float2 r;
       r.x = fminf(fmaxf(__fdiv_rn(f.x, s), -448.f), 448.f);
       r.y = fminf(fmaxf(__fdiv_rn(f.y, s), -448.f), 448.f);
       const __nv_fp8x2_storage_t p2 = __nv_cvt_float2_to_fp8x2(r, __NV_SATFINITE, __NV_E4M3);
-      packed[i >> 1] |= (uint32_t)p2 << (16 * (i & 1));
+      packed[j >> 1] |= (uint32_t)p2 << (16 * (j & 1));
     }
-    *reinterpret_cast<uint2*>(q + (size_t)m * K + v * 8) = make_uint2(packed[0], packed[1]);
+    *reinterpret_cast<uint2*>(q + (size_t)m * K + idx * 8) = make_uint2(packed[0], packed[1]);
   }
 }
 
@@ -203,17 +211,21 @@ extern "C" int cek_qkv_norm_rope(void* qkv, const int64_t* positions, const void
 
 extern "C" int cek_quant_fp8_per_token(const void* a, void* aq, float* a_scale, int64_t M,
                                        int64_t K, int dtype, void* stream) {
-  if (M < 0 || K <= 0 || K % 8 != 0 || M > INT32_MAX || K > INT32_MAX) return CEK_ERR_INVALID_ARG;
+  if (M < 0 || K <= 0 || K % 8 != 0 || K > 16384 || M > INT32_MAX) return CEK_ERR_INVALID_ARG;
   if (dtype != CEK_F16 && dtype != CEK_BF16) return CEK_ERR_INVALID_ARG;
   if (M == 0) return CEK_OK;
   if (!a || !aq || !a_scale) return CEK_ERR_INVALID_ARG;
   if (!cek_host::aligned16(a) || (reinterpret_cast<uintptr_t>(aq) & 7u)) return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == CEK_F16)
-    cek::quant_fp8_per_token_kernel<__half><<<(unsigned)M, 256, 0, st>>>(
-        static_cast<const __half*>(a), static_cast<uint8_t*>(aq), a_scale, (int)K);
-  else
-    cek::quant_fp8_per_token_kernel<__nv_bfloat16><<<(unsigned)M, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(a), static_cast<uint8_t*>(aq), a_scale, (int)K);
+  const int vpt = (int)((K / 8 + 255) / 256);
+#define CEK_QUANT(T, V)                                                                      \
+  cek::quant_fp8_per_token_kernel<T, V><<<(unsigned)M, 256, 0, st>>>(                       \
+      static_cast<const T*>(a), static_cast<uint8_t*>(aq), a_scale, (int)K)
+#define CEK_QUANT_V(T)                                                                       \
+  if (vpt <= 1) CEK_QUANT(T, 1); else if (vpt <= 2) CEK_QUANT(T, 2);                         \
+  else if (vpt <= 4) CEK_QUANT(T, 4); else CEK_QUANT(T, 8);
+  if (dtype == CEK_F16) { CEK_QUANT_V(__half) } else { CEK_QUANT_V(__nv_bfloat16) }
+#undef CEK_QUANT_V
+#undef CEK_QUANT
   return cek_host::launch_status();
 }

@@ -154,7 +154,7 @@ CEK_API int cek_qkv_norm_rope(void* qkv, const int64_t* positions, const void* q
 
 /* ---- per-token dynamic e4m3 quantisation ----------------------------------
  * s[m] = max(amax(|a[m, :]|), 1e-12) / 448;  aq[m, k] = e4m3_rn(clamp(a / s[m])).
- * a: [M, K] fp16/bf16; aq: [M, K] e4m3; s: fp32 [M].  K % 8 == 0.
+ * a: [M, K] fp16/bf16; aq: [M, K] e4m3; s: fp32 [M].  K % 8 == 0, K <= 16384.
  * No reference counterpart (the reference GEMM takes fp16 activations). */
 CEK_API int cek_quant_fp8_per_token(const void* a, void* aq, float* a_scale, int64_t M,
                             int64_t K, int dtype, void* stream);

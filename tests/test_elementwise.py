@@ -40,7 +40,7 @@ def test_qkv_norm_rope(ext, cuda_device, hq, hkv, D, neox, io):
     O.assert_parity(qc[:, :v0], ref[:, :v0], f"hq={hq} hkv={hkv} D={D} neox={neox}")
 
 
-@pytest.mark.parametrize("M,K", [(1, 4096), (2048, 4096), (5, 8), (33, 1000)])
+@pytest.mark.parametrize("M,K", [(1, 4096), (2048, 4096), (5, 8), (33, 1000), (7, 8192), (3, 16384)])
 @pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
 def test_quant_fp8_per_token_bit_exact(ext, cuda_device, M, K, io):
     torch.manual_seed(2)

@@ -337,62 +337,70 @@ def run_ours(args, rank, world, local):
 
 def measure_chain(dev, rank: int, world: int, Ms=(1, 8), reps: int = 200) -> dict:
     """the 70B-shaped decode step (esimd_learning_b200.chain)
-    tensor-parallel over the `world` ranks of this run (NCCL all-reduce of the
-    down projection).  L layers with distinct weights are captured in one CUDA
-    graph so that each replay streams more than 3x L2 of weights per rank;
-    time = max over ranks of the CUDA-event time per layer-step."""
+    tensor-parallel over the `world` ranks of this run.  At TP > 1 the down
+    projection's all-reduce runs two ways: fused into the GEMV over NVLink
+    peer memory (cek_gemv_fp8_allreduce, "fused") and as GEMV + NCCL
+    all-reduce ("nccl").  L layers with distinct weights are captured in one
+    CUDA graph so that each replay streams more than 3x L2 of weights per
+    rank; time = max over ranks of the CUDA-event time per layer-step."""
     import esimd_learning_b200 as ops
-    from esimd_learning_b200.chain import ChainShape, DecodeChain, full_weights, shard_weights
+    from esimd_learning_b200.chain import ChainShape, DecodeChain, TPComm, full_weights, shard_weights
 
     shape = ChainShape()
     per_rank = shape.weight_bytes() // world
     layers = max(1, -(-(3 * 126 * 2**20) // per_rank))
     old = ops.esimd_set_weight_prefetch(True)
-    chains = {M: [] for M in Ms}
+    comm = TPComm(max(Ms) * shape.hidden, rank, world, dev) if world > 1 else None
+    modes = ["fused", "nccl"] if world > 1 else ["local"]
+    shards = []
     for l in range(layers):
         full = full_weights(shape, seed=100 + l, device=dev)
-        sh = shard_weights(full, shape, rank, world)
+        shards.append(shard_weights(full, shape, rank, world))
         del full
-        for M in Ms:
-            chains[M].append(DecodeChain(sh, shape, M, dev, group=None, world=world))
-        del sh
         torch.cuda.empty_cache()
     res = {"tp": world, "layers_per_replay": layers, "weight_bytes_per_rank_per_step": per_rank}
     peak, _ = peaks()
-    for M in Ms:
-        g = torch.Generator(device=dev).manual_seed(7)
-        h = torch.randn(M, shape.hidden, device=dev, generator=g).half()
-        r = torch.randn(M, shape.hidden, device=dev, generator=g).half()
-        a = torch.randn(M, shape.hidden, device=dev, generator=g).half()
-        pos = torch.randint(0, shape.max_position, (M,), device=dev, generator=g)
-        st = torch.cuda.Stream(dev)
-        with torch.cuda.stream(st):
-            for c in chains[M]:
-                c.step(h, r, a, pos)  # warm-up outside capture (NCCL, modules)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=st):
-                for c in chains[M]:
-                    c.step(h, r, a, pos)
-            for _ in range(5):
-                graph.replay()
-            torch.cuda.synchronize()
+    for mode in modes:
+        for M in Ms:
+            chains = [DecodeChain(sh, shape, M, dev, world=world, comm=comm if mode == "fused" else None)
+                      for sh in shards]
+            g = torch.Generator(device=dev).manual_seed(7)
+            h = torch.randn(M, shape.hidden, device=dev, generator=g).half()
+            r = torch.randn(M, shape.hidden, device=dev, generator=g).half()
+            a = torch.randn(M, shape.hidden, device=dev, generator=g).half()
+            pos = torch.randint(0, shape.max_position, (M,), device=dev, generator=g)
+            st = torch.cuda.Stream(dev)
+            with torch.cuda.stream(st):
+                for c in chains:
+                    c.step(h, r, a, pos)  # warm-up outside capture (NCCL, modules)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=st):
+                    for c in chains:
+                        c.step(h, r, a, pos)
+                for _ in range(5):
+                    graph.replay()
+                torch.cuda.synchronize()
+                barrier(world)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(st)
+                torch.cuda.synchronize()
             barrier(world)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            for _ in range(reps):
-                graph.replay()
-            e1.record(st)
-            torch.cuda.synchronize()
-        barrier(world)
-        us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (reps * layers), world)
-        gbs = per_rank / (us * 1e-6) / 1e9
-        res[f"M{M}"] = {"us_per_step": round(us, 2), "weight_gbs_per_gpu": round(gbs, 1),
+            us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (reps * layers), world)
+            gbs = per_rank / (us * 1e-6) / 1e9
+            key = f"M{M}" if mode in ("fused", "local") else f"M{M}_nccl"
+            res[key] = {"us_per_step": round(us, 2), "weight_gbs_per_gpu": round(gbs, 1),
                         "frac_of_hbm": round(gbs / peak, 4),
-                        "kernels_per_step": 7, "nccl_all_reduce": world > 1}
-        del graph
+                        "all_reduce": {"fused": "GEMV push over NVLink peer memory + reduce kernel",
+                                       "nccl": "NCCL all_reduce", "local": "none (TP=1)"}[mode]}
+            del graph, chains
+    if comm is not None:
+        res["comm_errors"] = comm.errors()
+        comm.close()
     ops.esimd_set_weight_prefetch(old)
-    del chains
     torch.cuda.empty_cache()
     return res
 

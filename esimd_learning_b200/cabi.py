@@ -40,6 +40,14 @@ SIGNATURES = {
     "cek_gelu_and_mul": (_I, [_P, _P, _I64, _I64, _I, _P]),
     "cek_qkv_norm_rope": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I, _I, _P]),
     "cek_quant_fp8_per_token": (_I, [_P, _P, _P, _I64, _I64, _I, _P]),
+    "cek_tp_comm_bytes": (_I64, [_I64, _I]),
+    "cek_comm_alloc": (_I, [_I64, ctypes.POINTER(ctypes.c_void_p)]),
+    "cek_comm_free": (_I, [_P]),
+    "cek_ipc_get_handle": (_I, [_P, ctypes.c_char_p]),
+    "cek_ipc_open_handle": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "cek_ipc_close_handle": (_I, [_P]),
+    "cek_comm_errors": (_I, [_P, ctypes.POINTER(ctypes.c_uint32)]),
+    "cek_gemv_fp8_allreduce": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _I64, _I, _I, _U, _P]),
     "cek_gemm_fp8_scaled": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "cek_gemm_fp8_timeouts": (_I, [ctypes.POINTER(ctypes.c_uint64)]),
 }

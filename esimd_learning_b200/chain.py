@@ -119,14 +119,73 @@ def rope_cache(shape: ChainShape, device) -> torch.Tensor:
     return torch.cat([fr.cos(), fr.sin()], dim=-1).to(device)
 
 
+class TPComm:
+    """Peer-memory plumbing for the fused down-projection all-reduce
+    (cek_gemv_fp8_allreduce): this rank's comm region (cek_comm_alloc), its
+    CUDA IPC handle exchanged over `group`, the peers' regions mapped into
+    this process, and a device array of all regions' addresses.  Set-up only
+    (allocates, maps, synchronises); the per-step call does neither."""
+
+    def __init__(self, slot_elems: int, rank: int, world: int, device, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from esimd_learning_b200 import cabi
+
+        self.cabi, self.rank, self.world, self.slot_elems = cabi, rank, world, slot_elems
+        L = cabi.lib()
+        nbytes = L.cek_tp_comm_bytes(slot_elems, world)
+        if nbytes <= 0:
+            raise ValueError("bad comm size")
+        mine = ctypes.c_void_p()
+        cabi.call("cek_comm_alloc", nbytes, ctypes.byref(mine))
+        self.mine = mine.value
+        handle = ctypes.create_string_buffer(64)
+        cabi.call("cek_ipc_get_handle", self.mine, handle)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.opened = []
+        addrs = []
+        for r, h in enumerate(handles):
+            if r == rank:
+                addrs.append(self.mine)
+            else:
+                p = ctypes.c_void_p()
+                cabi.call("cek_ipc_open_handle", h, ctypes.byref(p))
+                self.opened.append(p.value)
+                addrs.append(p.value)
+        self.peers = torch.tensor(addrs, dtype=torch.int64, device=device)
+        dist.barrier(group=group)
+
+    def errors(self) -> int:
+        import ctypes
+        v = ctypes.c_uint32(0)
+        self.cabi.call("cek_comm_errors", self.mine, ctypes.byref(v))
+        return v.value
+
+    def close(self):
+        for p in self.opened:
+            self.cabi.lib().cek_ipc_close_handle(p)
+        self.opened = []
+        if self.mine:
+            self.cabi.lib().cek_comm_free(self.mine)
+            self.mine = None
+
+
 class DecodeChain:
     """One rank's executor of the decode step (module docstring).  `group`
-    is the torch.distributed process group of the TP ranks (None at TP=1)."""
+    is the torch.distributed process group of the TP ranks (None at TP=1).
+    With `comm` (a TPComm) the down projection and its all-reduce run as the
+    fused peer-memory pair of cek_gemv_fp8_allreduce instead of a GEMV
+    followed by an NCCL all-reduce."""
 
-    def __init__(self, shards: dict, shape: ChainShape, M: int, device, group=None, world: int = 1):
+    def __init__(self, shards: dict, shape: ChainShape, M: int, device, group=None, world: int = 1,
+                 comm: "TPComm | None" = None):
         import esimd_learning_b200 as ops
 
         self.ops, self.shape, self.M, self.dev, self.group, self.world = ops, shape, M, device, group, world
+        self.comm = comm
         self.w = {k: (tuple(t.to(device) for t in v) if isinstance(v, tuple) else
                       (v.to(device) if torch.is_tensor(v) else v)) for k, v in shards.items()}
         lq, lkv, lf = shards["local_q_heads"], shards["local_kv_heads"], shards["local_intermediate"]
@@ -151,6 +210,12 @@ class DecodeChain:
                                                self.gu)
         o.esimd_gelu_and_mul(self.gu, self.act)
         wd, sd = w["down"]
+        if self.world > 1 and self.comm is not None:
+            c, cb = self.comm, self.comm.cabi
+            cb.call("cek_gemv_fp8_allreduce", cb.ptr(self.act), cb.ptr(wd), cb.ptr(sd), cb.ptr(self.out),
+                    self.M, s.hidden, self.lf, cb.CEK_F16, cb.CEK_E4M3, cb.CEK_SCALE_PERN_F32, cb.ptr(c.peers),
+                    c.mine, c.slot_elems, c.rank, c.world, 0, cb.current_stream())
+            return self.out, self.qkv
         o.esimd_gemv_fp8_pern(self.act, wd, sd, self.out, s.hidden, self.lf)
         if self.world > 1:
             import torch.distributed as dist

@@ -24,7 +24,34 @@ struct GemvParams {
   // guarantees the preceding kernel on the stream does not write them);
   // 0: every global read waits for the preceding kernel.
   int early_weights;
+  // tensor-parallel all-reduce epilogue (ar_world > 0, tp_allreduce.cu):
+  // y is pushed into slot ar_rank of every rank's receive buffer instead of
+  // being stored to p.y.
+  const unsigned long long* ar_peers;  // device array [ar_world] of comm base addresses
+  unsigned* ar_sync;                   // this rank's sync block
+  int ar_rank, ar_world;
 };
+
+// Layout of a rank's tensor-parallel comm region: a 4 KiB sync block
+// (32-bit words) followed by two sets of ar_world receive slots of M*N
+// elements (set = epoch parity).
+namespace tp {
+constexpr int kSyncBytes = 4096;
+constexpr int kMaxRanks = 64;
+constexpr int kReady = 0;        // [kMaxRanks] epoch at which peer r pushed its slot
+constexpr int kEpoch = 128;      // last completed epoch of this rank
+constexpr int kReduceCount = 130;  // CTAs of the reduce kernel that finished
+constexpr int kErrors = 131;     // bit 0: a bounded wait gave up
+}  // namespace tp
+
+CEK_DEVICE void st_release_sys(unsigned* addr, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+CEK_DEVICE unsigned ld_acquire_sys(const unsigned* addr) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
 
 // ---- device helpers shared by both GEMV kernels ----------------------------------
 

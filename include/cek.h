@@ -159,6 +159,36 @@ CEK_API int cek_qkv_norm_rope(void* qkv, const int64_t* positions, const void* q
 CEK_API int cek_quant_fp8_per_token(const void* a, void* aq, float* a_scale, int64_t M,
                             int64_t K, int dtype, void* stream);
 
+/* ---- tensor parallel: row-parallel FP8 GEMV fused with its all-reduce -----
+ * out[m, n] = sum over the `world` ranks of GEMV(x_r, w_r, scale)[m, n],
+ * every rank getting the same bits.  Each rank owns a comm region of
+ * cek_tp_comm_bytes(slot_elems, world) bytes from cek_comm_alloc (zeroed);
+ * ranks exchange its CUDA IPC handle (cek_ipc_get_handle / cek_ipc_open_handle)
+ * and pass `peer_comm`, a DEVICE array of `world` 64-bit addresses of every
+ * rank's region as mapped in this process (own region at index rank).
+ * The GEMV's epilogue pushes its tiles into every rank's region over NVLink
+ * while later tiles are still computing; a second small kernel raises this
+ * rank's ready flag on every rank, waits for all ranks' flags (bounded), adds
+ * the slots in rank order and writes `out`.
+ * M * N <= slot_elems; K % 16 == 0; one call at a time per region.
+ * Bounded waits that run out set bit 0 of the region's error word
+ * (cek_comm_errors).  No reference counterpart: the reference is single-GPU.
+ * cek_comm_alloc / cek_comm_free / the IPC calls are set-up calls (they
+ * allocate or map memory and synchronise); the GEMV call does neither. */
+#define CEK_IPC_HANDLE_BYTES 64
+CEK_API int64_t cek_tp_comm_bytes(int64_t slot_elems, int world);
+CEK_API int cek_comm_alloc(int64_t bytes, void** ptr);
+CEK_API int cek_comm_free(void* ptr);
+CEK_API int cek_ipc_get_handle(void* ptr, void* handle);
+CEK_API int cek_ipc_open_handle(const void* handle, void** ptr);
+CEK_API int cek_ipc_close_handle(void* ptr);
+CEK_API int cek_comm_errors(void* my_comm, uint32_t* out);
+CEK_API int cek_gemv_fp8_allreduce(const void* x, const void* w, const void* scale, void* out,
+                                   int64_t M, int64_t N, int64_t K, int dtype, int w_fmt,
+                                   int scale_kind, const uint64_t* peer_comm, void* my_comm,
+                                   int64_t slot_elems, int rank, int world, unsigned flags,
+                                   void* stream);
+
 /* ---- FP8 x FP8 GEMM, per-token x per-channel scales (tcgen05) -------------
  * y[m, n] = OutT( (sum_k deq(aq[m, k]) * deq(bq[n, k])) * a_scale[m] * b_scale[n] )
  * aq: [M, K] e4m3 (e.g. from cek_quant_fp8_per_token); bq: [N, K] e4m3;

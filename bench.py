@@ -565,6 +565,22 @@ def _claim_stdout():
     return os.fdopen(real, "w")
 
 
+def profile_chain(M: int):
+    """Two eager steps of the TP=1 decode chain of BASELINE config 4 (7 kernels
+    each, 788 MB of weights)."""
+    from esimd_learning_b200.chain import ChainShape, DecodeChain, full_weights, shard_weights
+    dev = torch.device("cuda", 0)
+    shape = ChainShape()
+    chain = DecodeChain(shard_weights(full_weights(shape, seed=0, device=dev), shape, 0, 1), shape, M, dev)
+    torch.cuda.empty_cache()
+    h, r, a = (torch.randn(M, shape.hidden, device=dev).half() for _ in range(3))
+    pos = torch.randint(0, shape.max_position, (M,), device=dev)
+    for _ in range(2):
+        chain.step(h, r, a, pos)
+    torch.cuda.synchronize()
+    print("profile chain done")
+
+
 def profile_gemm(M: int):
     """Two launches each of the per-token quantisation and the tcgen05 GEMM of
     BASELINE config 3 at this M (A [M, 4096], B [14336, 4096])."""
@@ -594,6 +610,8 @@ def main():
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
     ap.add_argument("--no-chain", action="store_true", help="skip the config-4 decode-chain measurement")
     ap.add_argument("--no-prefetch", action="store_true", help="GEMVs wait for the previous kernel before any load")
+    ap.add_argument("--profile-chain", type=int, default=0, metavar="M",
+                    help="run two eager TP=1 decode-chain steps (config 4) at this M and exit; for ncu")
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="M",
                     help="run quant + tcgen05 GEMM of config 3 at this M twice and exit; for ncu")
     ap.add_argument("--profile", action="store_true",
@@ -604,6 +622,9 @@ def main():
         return
     if args.profile_gemm:
         profile_gemm(args.profile_gemm)
+        return
+    if args.profile_chain:
+        profile_chain(args.profile_chain)
         return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -34,7 +34,7 @@ SIGNATURES = {
     "cek_version": (ctypes.c_char_p, []),
     "cek_gemv_fp8": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _I, _U, _P]),
     "cek_fused_add_rmsnorm": (_I, [_P, _P, _P, _I64, _I64, _F, _I, _P]),
-    "cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes": (_I64, [_I64]),
+    "cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes": (_I64, [_I64, _I64]),
     "cek_fused_add_rmsnorm_gemv_fp8": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _U, _P]),
     "cek_fused_add_rmsnorm_gemv_fp8_noalloc": (_I, [_P, _P, _P, _F, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _U, _P]),
     "cek_gelu_and_mul": (_I, [_P, _P, _I64, _I64, _I, _P]),

@@ -38,15 +38,20 @@ CEK_DEVICE float block_sum(float v, float* sh) {
   return sh[0];
 }
 
-// VPT = 16-byte vectors per thread.  WRITE_NORMED: standalone op (writes the
-// normalised row into hidden).  Otherwise it is the GEMV prologue and only
-// the per-row inverse RMS is written (to inv_rms[row]).
-template <typename T, int VPT, bool WRITE_NORMED>
+// What the kernel writes besides the updated residual.
+enum NormMode {
+  kNormedInPlace = 0,  // standalone op: the normalised row into hidden
+  kInvRmsOnly = 1,     // GEMV prologue: the per-row inverse RMS only
+  kNormedOut = 2,      // GEMV prologue: the normalised row into a scratch row
+};
+
+// VPT = 16-byte vectors per thread.
+template <typename T, int VPT, int MODE>
 __global__ void __launch_bounds__(kNormThreads)
 add_rmsnorm_kernel(T* hidden, T* residual, const T* __restrict__ weight, float* inv_rms_out,
-                   int K, float eps) {
+                   T* normed_out, int K, float eps) {
   __shared__ float sh[32];
-  if constexpr (!WRITE_NORMED) pdl_launch_dependents();
+  if constexpr (MODE != kNormedInPlace) pdl_launch_dependents();
   const int row = blockIdx.x;
   const int nvec = K >> 3;
   uint4* hrow = reinterpret_cast<uint4*>(hidden + (size_t)row * K);
@@ -72,9 +77,10 @@ add_rmsnorm_kernel(T* hidden, T* residual, const T* __restrict__ weight, float* 
   }
   const float total = block_sum<T>(ss, sh);
   const float inv = rsqrtf(total / (float)K + eps);
-  if constexpr (!WRITE_NORMED) {
+  if constexpr (MODE == kInvRmsOnly) {
     if (threadIdx.x == 0) inv_rms_out[row] = inv;
   } else {
+    uint4* orow = reinterpret_cast<uint4*>((MODE == kNormedInPlace ? hidden : normed_out) + (size_t)row * K);
     const uint4* wv = reinterpret_cast<const uint4*>(weight);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -88,14 +94,14 @@ add_rmsnorm_kernel(T* hidden, T* residual, const T* __restrict__ weight, float* 
           float2 rf = unpack2<T>(rw[q]), wf = unpack2<T>(ww[q]);
           ow[q] = pack2<T>(rf.x * inv * wf.x, rf.y * inv * wf.y);
         }
-        hrow[v] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        orow[v] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
     }
   }
 }
 
-template <typename T, bool WRITE_NORMED>
-static int launch_norm(void* hidden, void* residual, const void* weight, float* inv_rms,
+template <typename T, int MODE>
+static int launch_norm(void* hidden, void* residual, const void* weight, float* inv_rms, void* normed,
                        int64_t rows, int64_t K, float eps, cudaStream_t st) {
   const int nvec = (int)(K / 8);
   const int vpt = (nvec + kNormThreads - 1) / kNormThreads;
@@ -105,7 +111,8 @@ static int launch_norm(void* hidden, void* residual, const void* weight, float* 
   const T* w = static_cast<const T*>(weight);
 #define CEK_NORM(V)                                                                              \
   if (vpt <= V) {                                                                                \
-    add_rmsnorm_kernel<T, V, WRITE_NORMED><<<grid, block, 0, st>>>(h, r, w, inv_rms, (int)K, eps); \
+    add_rmsnorm_kernel<T, V, MODE><<<grid, block, 0, st>>>(h, r, w, inv_rms, static_cast<T*>(normed), \
+                                                           (int)K, eps);                                 \
     return cek_host::launch_status();                                                            \
   }
   CEK_NORM(1) CEK_NORM(2) CEK_NORM(4) CEK_NORM(8)
@@ -134,17 +141,24 @@ extern "C" int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* w
   if (!cek_host::aligned16(weight)) return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == CEK_F16)
-    return cek::launch_norm<__half, true>(hidden, residual, weight, nullptr, rows, K, eps, st);
-  return cek::launch_norm<__nv_bfloat16, true>(hidden, residual, weight, nullptr, rows, K, eps, st);
+    return cek::launch_norm<__half, cek::kNormedInPlace>(hidden, residual, weight, nullptr, nullptr, rows, K,
+                                                         eps, st);
+  return cek::launch_norm<__nv_bfloat16, cek::kNormedInPlace>(hidden, residual, weight, nullptr, nullptr, rows,
+                                                                K, eps, st);
 }
 
-// Workspace: the per-row inverse RMS written by the stats kernel and read by
-// the GEMV (M floats, padded to 256 bytes).
+// Workspace.  With at least cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, K)
+// bytes the stats kernel writes the normalised rows (M x K, I/O dtype, an
+// L2-resident scratch) and the GEMV runs its plain operand path on them.
+// With only the 256-byte inverse-RMS block the stats kernel writes the
+// per-row inverse RMS and the GEMV forms the normalised operand inside its
+// loads (slower: every warp redoes the scaling).
 static int64_t inv_rms_bytes(int64_t M) { return ((M * (int64_t)sizeof(float) + 255) / 256) * 256; }
+static int64_t normed_bytes(int64_t M, int64_t K) { return ((M * K * 2 + 255) / 256) * 256; }
 
-extern "C" int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M) {
-  if (M <= 0 || M > 16) return 0;
-  return inv_rms_bytes(M);
+extern "C" int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M, int64_t K) {
+  if (M <= 0 || M > 16 || K <= 0 || K > 16384) return 0;
+  return normed_bytes(M, K);
 }
 
 extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual,
@@ -165,20 +179,32 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
   if (!cek_host::aligned16(norm_weight) || !cek_host::aligned16(w) || !cek_host::aligned16(workspace))
     return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool staged = workspace_bytes >= normed_bytes(M, K);
   float* inv = static_cast<float*>(workspace);
   // The stats kernel only reads `hidden`; the const_cast never leads to a write.
   void* h = const_cast<void*>(hidden);
-  s = dtype == CEK_F16
-          ? cek::launch_norm<__half, false>(h, residual, nullptr, inv, M, K, eps, st)
-          : cek::launch_norm<__nv_bfloat16, false>(h, residual, nullptr, inv, M, K, eps, st);
+  if (staged)
+    s = dtype == CEK_F16
+            ? cek::launch_norm<__half, cek::kNormedOut>(h, residual, norm_weight, nullptr, workspace, M, K, eps, st)
+            : cek::launch_norm<__nv_bfloat16, cek::kNormedOut>(h, residual, norm_weight, nullptr, workspace, M, K,
+                                                               eps, st);
+  else
+    s = dtype == CEK_F16
+            ? cek::launch_norm<__half, cek::kInvRmsOnly>(h, residual, nullptr, inv, nullptr, M, K, eps, st)
+            : cek::launch_norm<__nv_bfloat16, cek::kInvRmsOnly>(h, residual, nullptr, inv, nullptr, M, K, eps, st);
   if (s != CEK_OK || N == 0) return s;
   cek::GemvParams p = {};
-  p.x = nullptr; p.w = static_cast<const uint8_t*>(w); p.scale = scale; p.y = y;
+  p.w = static_cast<const uint8_t*>(w); p.scale = scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
-  p.residual = residual; p.gamma = norm_weight; p.inv_rms = inv;
   // The stats kernel never writes W: the GEMV may always prefetch it.
   p.early_weights = 1;
   (void)flags;
+  if (staged) {
+    p.x = workspace;
+    return cek::gemv_launch(p, dtype, dtype, w_fmt, scale_kind, false, st);
+  }
+  p.x = nullptr;
+  p.residual = residual; p.gamma = norm_weight; p.inv_rms = inv;
   return cek::gemv_launch(p, dtype, dtype, w_fmt, scale_kind, true, st);
 }
 

@@ -116,8 +116,8 @@ at::Tensor esimd_fused_add_rms_norm_batched_fp8(at::Tensor hidden_states, at::Te
   const int sk = scale_kind(qweight_scale, N, true, op);
   c10::cuda::CUDAGuard guard(hidden_states.device());
   TORCH_CHECK(M <= 16, op, ": at most 16 rows");
-  // per-row inverse RMS: a few bytes from the caching allocator (graph-safe)
-  const int64_t ws_bytes = cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M);
+  // normalised rows (M x K): a small caching-allocator block (graph-safe)
+  const int64_t ws_bytes = cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, K);
   at::Tensor ws = at::empty({ws_bytes}, hidden_states.options().dtype(at::kByte));
   check_status(cek_fused_add_rmsnorm_gemv_fp8(
                    hidden_states.data_ptr(), residual.data_ptr(), weight.data_ptr(), (float)eps,

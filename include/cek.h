@@ -88,18 +88,21 @@ CEK_API int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* weig
 
 /* ---- residual add + RMSNorm fused into an FP8 GEMV ------------------------
  * residual = io(hidden + residual)  (in place; hidden is not written)
- * xn       = io(f32(residual) * inv_rms[m] * weight)   (stays on chip)
+ * xn       = io(f32(residual) * inv_rms[m] * weight)
  * y        = GEMV(xn, w, scale)  as cek_gemv_fp8.
  * Two launches chained by programmatic dependent launch: a per-row stats
- * kernel (residual update, inverse RMS into `workspace`) and the GEMV, which
- * forms xn in its operand loads and streams w while the stats kernel runs.
- * workspace: device scratch of at least
- * cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M) bytes, contents ignored.
+ * kernel (residual update and normalisation) and the GEMV, which streams w
+ * while the stats kernel runs.
+ * workspace (contents ignored):
+ *   >= cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, K) bytes: the stats
+ *      kernel writes xn there (M x K, L2-resident) and the GEMV reads it;
+ *   >= 256 bytes only: the stats kernel writes the per-row inverse RMS and
+ *      the GEMV forms xn inside its operand loads (slower).
  * flags: reserved for CEK_GEMV_EARLY_WEIGHTS (the weight stream always
  * starts early here: the stats kernel never writes w).
  * M <= 16, K % 8 == 0, K <= 16384.  No reference counterpart: the reference
  * runs fused_add_rms_norm_batched_host and GEMV_fp8_pern_host as two ops. */
-CEK_API int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M);
+CEK_API int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M, int64_t K);
 CEK_API int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual,
                                            const void* norm_weight, float eps,
                                            const void* w, const void* scale, void* y,

@@ -56,8 +56,8 @@ def test_norm_and_helpers_reject_bad_arguments():
     assert L.cek_fused_add_rmsnorm(16, 16, 16, 1, 32768, 1e-6, 0, None) == cabi.CEK_ERR_INVALID_ARG
     assert L.cek_fused_add_rmsnorm(16, 16, 16, 0, 512, 1e-6, 0, None) == cabi.CEK_OK
     assert L.cek_fused_add_rmsnorm(8, 16, 16, 1, 512, 1e-6, 0, None) == cabi.CEK_ERR_ALIGNMENT
-    assert L.cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(3) == 256
-    assert L.cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(17) == 0
+    assert L.cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(3, 512) == 3072
+    assert L.cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(17, 512) == 0
     assert L.cek_fused_add_rmsnorm_gemv_fp8(16, 16, 16, 1e-6, 16, 16, 16, 16, 1 << 20, 17, 64, 512, 0,
                                             0, 0, 0, None) == cabi.CEK_ERR_INVALID_ARG
     # workspace smaller than the inverse-RMS block

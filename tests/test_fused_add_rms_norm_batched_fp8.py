@@ -85,7 +85,7 @@ def test_fused_matches_unfused_composition(ext, cuda_device):
 def test_fused_through_cabi(cuda_device):
     h, r, g, wq, s = fused_norm_case(3, N=200, K=1024, seed=9, device=cuda_device)
     ref_r, ref_y = O.add_rmsnorm_gemv_fp8(h.cpu(), r.cpu(), g.cpu(), 1e-6, wq.cpu(), s.cpu())
-    nbytes = cabi.lib().cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(3)
+    nbytes = cabi.lib().cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(3, 1024)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device)
     y = torch.zeros(3, 200, dtype=torch.float16, device=cuda_device)
     cabi.call("cek_fused_add_rmsnorm_gemv_fp8", cabi.ptr(h), cabi.ptr(r), cabi.ptr(g), 1e-6,
@@ -94,3 +94,26 @@ def test_fused_through_cabi(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(r.cpu(), ref_r)
     O.assert_parity(y, ref_y, "cabi fused")
+
+
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_fused_both_workspace_paths(cuda_device, io):
+    """Full workspace: the normalised rows are staged for the GEMV; a 256-byte
+    workspace: the GEMV forms them inside its loads.  Same residual, outputs
+    within tolerance of each other and of the oracle."""
+    M, N, K = 5, 3000, 4096
+    h, r, g, wq, s = fused_norm_case(M, N=N, K=K, seed=13, dtype=io, device=cuda_device)
+    ref_r, ref_y = O.add_rmsnorm_gemv_fp8(h.cpu(), r.cpu(), g.cpu(), 1e-6, wq.cpu(), s.cpu())
+    outs = []
+    for nbytes in (cabi.lib().cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, K), 256):
+        rr = r.clone()
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device)
+        y = torch.zeros(M, N, dtype=io, device=cuda_device)
+        cabi.call("cek_fused_add_rmsnorm_gemv_fp8", cabi.ptr(h), cabi.ptr(rr), cabi.ptr(g), 1e-6, cabi.ptr(wq),
+                  cabi.ptr(s), cabi.ptr(y), cabi.ptr(ws), nbytes, M, N, K, cabi.io_dtype(h), cabi.CEK_E4M3,
+                  cabi.CEK_SCALE_PERN_F32, 0, cabi.current_stream())
+        torch.cuda.synchronize()
+        assert torch.equal(rr.cpu(), ref_r)
+        O.assert_parity(y, ref_y, f"workspace {nbytes}")
+        outs.append(y)
+    O.assert_parity(outs[0], outs[1].cpu(), "staged vs in-load")

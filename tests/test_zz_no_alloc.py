@@ -25,7 +25,7 @@ def _run(entry, h, r, g, wq, s, M, N, K):
     y = torch.zeros(M, N, dtype=h.dtype, device=h.device)
     args = [cabi.ptr(h), cabi.ptr(r), cabi.ptr(g), 1e-6, cabi.ptr(wq), cabi.ptr(s), cabi.ptr(y)]
     if entry == "cek_fused_add_rmsnorm_gemv_fp8":
-        nbytes = cabi.lib().cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M)
+        nbytes = cabi.lib().cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, K)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=h.device)
         args += [cabi.ptr(ws), nbytes]
     args += [M, N, K, cabi.io_dtype(h), cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, 0,

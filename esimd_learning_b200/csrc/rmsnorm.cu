@@ -8,8 +8,8 @@
 //   pass 2  hidden = fp16(f32(residual_fp16) * inv_rms * w)      (:56-62)
 // with inv_rms = rsqrt(sum / K + eps) and w the pre-shifted (w + 1) weight.
 //
-// B200 layout: one CTA per row, 256 threads, each thread keeps its 8..64
-// elements of the row in registers between the two passes, so the row is read
+// B200 layout: one CTA per row, up to 1024 threads, each thread keeps its
+// 8..64 elements of the row in registers between the two passes, so the row is read
 // once from HBM and written once (the reference re-reads the residual in
 // pass 2).  16-byte vector loads/stores; warp-shuffle + shared-memory
 // reduction.  Requires K % 8 == 0 and K <= 16384 (the reference requires
@@ -20,7 +20,7 @@
 
 namespace cek {
 
-constexpr int kNormThreads = 256;
+constexpr int kNormMaxThreads = 1024;
 
 template <typename T>
 CEK_DEVICE float block_sum(float v, float* sh) {
@@ -47,7 +47,7 @@ enum NormMode {
 
 // VPT = 16-byte vectors per thread.
 template <typename T, int VPT, int MODE>
-__global__ void __launch_bounds__(kNormThreads)
+__global__ void __launch_bounds__(kNormMaxThreads)
 add_rmsnorm_kernel(T* hidden, T* residual, const T* __restrict__ weight, float* inv_rms_out,
                    T* normed_out, int K, float eps) {
   __shared__ float sh[32];
@@ -60,7 +60,7 @@ add_rmsnorm_kernel(T* hidden, T* residual, const T* __restrict__ weight, float* 
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    const int v = threadIdx.x + i * kNormThreads;
+    const int v = threadIdx.x + i * blockDim.x;
     if (v < nvec) {
       uint4 h = hrow[v], r = rrow[v];
       uint32_t hw[4] = {h.x, h.y, h.z, h.w}, rw[4] = {r.x, r.y, r.z, r.w}, ow[4];
@@ -84,7 +84,7 @@ add_rmsnorm_kernel(T* hidden, T* residual, const T* __restrict__ weight, float* 
     const uint4* wv = reinterpret_cast<const uint4*>(weight);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-      const int v = threadIdx.x + i * kNormThreads;
+      const int v = threadIdx.x + i * blockDim.x;
       if (v < nvec) {
         uint4 w4 = wv[v];
         uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
@@ -103,9 +103,11 @@ add_rmsnorm_kernel(T* hidden, T* residual, const T* __restrict__ weight, float* 
 template <typename T, int MODE>
 static int launch_norm(void* hidden, void* residual, const void* weight, float* inv_rms, void* normed,
                        int64_t rows, int64_t K, float eps, cudaStream_t st) {
+  // one 16-byte vector per thread up to 1024 threads, then 2, 4, 8 per thread
   const int nvec = (int)(K / 8);
-  const int vpt = (nvec + kNormThreads - 1) / kNormThreads;
-  dim3 grid((unsigned)rows), block(kNormThreads);
+  const int threads = nvec >= kNormMaxThreads ? kNormMaxThreads : ((nvec + 31) / 32) * 32;
+  const int vpt = (nvec + threads - 1) / threads;
+  dim3 grid((unsigned)rows), block(threads);
   T* h = static_cast<T*>(hidden);
   T* r = static_cast<T*>(residual);
   const T* w = static_cast<const T*>(weight);

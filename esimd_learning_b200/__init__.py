@@ -26,6 +26,7 @@ except ImportError as e:  # pragma: no cover - exercised only on an unbuilt tree
 from esimd_learning_b200.ops import (  # noqa: E402,F401
     esimd_gemv_fp8_pern,
     esimd_gemv_fp8_pert,
+    esimd_gemv_fp8_pern_fused,
     esimd_fused_add_rms_norm_batched,
     esimd_gemm_fp8_pert,
     esimd_fused_add_rms_norm_batched_fp8,

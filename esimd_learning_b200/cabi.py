@@ -33,6 +33,8 @@ SIGNATURES = {
     "cek_status_string": (ctypes.c_char_p, [_I]),
     "cek_version": (ctypes.c_char_p, []),
     "cek_gemv_fp8": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _I, _U, _P]),
+    "cek_gemv_fp8_multi": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P),
+                                ctypes.POINTER(_I64), _I, _I64, _I64, _I, _I, _I, _I, _U, _P]),
     "cek_fused_add_rmsnorm": (_I, [_P, _P, _P, _I64, _I64, _F, _I, _P]),
     "cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes": (_I64, [_I64, _I64]),
     "cek_fused_add_rmsnorm_gemv_fp8": (_I, [_P, _P, _P, _F, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _U, _P]),

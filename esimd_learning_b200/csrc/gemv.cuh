@@ -6,6 +6,8 @@
 
 namespace cek {
 
+constexpr int kMaxMats = 4;  // matrices per multi-GEMV launch
+
 struct GemvParams {
   const void* x;          // [M, K] activations (plain GEMV)
   const uint8_t* w;       // [N, K] fp8
@@ -30,6 +32,14 @@ struct GemvParams {
   const unsigned long long* ar_peers;  // device array [ar_world] of comm base addresses
   unsigned* ar_sync;                   // this rank's sync block
   int ar_rank, ar_world;
+  // several weight matrices sharing x in one launch (nmat > 0): matrix m
+  // owns CTAs [mcta_off[m], mcta_off[m+1]) and writes ys[m] [M, ns[m]]
+  int nmat;
+  const uint8_t* mws[kMaxMats];
+  const void* mscales[kMaxMats];
+  void* mys[kMaxMats];
+  int mns[kMaxMats];
+  int mcta_off[kMaxMats + 1];
 };
 
 // Layout of a rank's tensor-parallel comm region: a 4 KiB sync block

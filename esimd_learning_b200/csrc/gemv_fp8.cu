@@ -30,6 +30,7 @@
 //    the first batch of weight loads is issued before griddepcontrol.wait;
 //    activation loads and all stores always come after it.
 #include "gemv.cuh"
+#include <algorithm>
 #include <cstdlib>
 #include <type_traits>
 
@@ -109,12 +110,23 @@ CEK_DEVICE void consume(const Batch<NT>& b, float (&acc)[NT][4]) {
 
 template <typename InT, int FMT, int SCALE, typename OutT, int NT, bool FUSED>
 __global__ void __launch_bounds__(kMaxWarps * 32)
-gemv_fp8_kernel(const GemvParams p) {
+gemv_fp8_kernel(const GemvParams pin) {
   constexpr int U = Batch<NT>::U;
   __shared__ float red[kMaxWarps][16][NT * 8];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cta = blockIdx.x / p.mtiles, mt = blockIdx.x % p.mtiles;
+  GemvParams p = pin;
+  int cta = blockIdx.x / p.mtiles;
+  const int mt = blockIdx.x % p.mtiles;
+  if (p.nmat > 0) {  // multi-GEMV: pick this CTA's matrix
+    int m = 0;
+    while (m + 1 < p.nmat && cta >= p.mcta_off[m + 1]) ++m;
+    p.w = p.mws[m];
+    p.scale = p.mscales[m];
+    p.y = p.mys[m];
+    p.N = p.mns[m];
+    cta -= p.mcta_off[m];
+  }
   const int rg_local = warp / p.ks, kslice = warp % p.ks;
   WarpCtx<NT> c;
   c.g = lane >> 2;
@@ -271,9 +283,18 @@ static int dispatch_fmt_scale(const GemvParams& p, const GemvLaunch& L, int w_fm
 
 int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
                 bool fused, cudaStream_t st) {
-  GemvLaunch L = plan_gemv(base.M, base.N, base.K);
+  GemvLaunch L = plan_gemv(base.M, base.N, base.K);  // multi-GEMV: N = sum of the matrices' N
   GemvParams p = base;
   p.ks = L.ks; p.rg_per_cta = L.rg_per_cta; p.mtiles = L.mtiles; p.cpw = L.cpw;
+  if (p.nmat > 0) {
+    int64_t ctas = 0;
+    for (int m = 0; m < p.nmat; ++m) {
+      p.mcta_off[m] = (int)ctas;
+      ctas += ((int64_t)(p.mns[m] + 15) / 16 + L.rg_per_cta - 1) / L.rg_per_cta;
+    }
+    p.mcta_off[p.nmat] = (int)ctas;
+    L.ctas = ctas * L.mtiles;
+  }
   if (fused) {
     if (x_dtype != y_dtype) return CEK_ERR_INVALID_ARG;
     if (x_dtype == CEK_F16) return dispatch_fmt_scale<__half, __half, true>(p, L, w_fmt, scale_kind, st);
@@ -310,4 +331,40 @@ extern "C" int cek_gemv_fp8(const void* x, const void* w, const void* scale, voi
   p.early_weights = (flags & CEK_GEMV_EARLY_WEIGHTS) ? 1 : 0;
   return cek::gemv_launch(p, x_dtype, y_dtype, w_fmt, scale_kind, false,
                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cek_gemv_fp8_multi(const void* x, const void* const* ws, const void* const* scales,
+                                  void* const* ys, const int64_t* Ns, int count, int64_t M, int64_t K,
+                                  int x_dtype, int y_dtype, int w_fmt, int scale_kind, unsigned flags,
+                                  void* stream) {
+  using namespace cek_host;
+  if (count < 1 || count > cek::kMaxMats || !ws || !scales || !ys || !Ns) return CEK_ERR_INVALID_ARG;
+  if (M < 0 || K < 0 || K % 16 != 0 || M > INT32_MAX || K > INT32_MAX) return CEK_ERR_INVALID_ARG;
+  if ((x_dtype != CEK_F16 && x_dtype != CEK_BF16) || (y_dtype != CEK_F16 && y_dtype != CEK_BF16))
+    return CEK_ERR_INVALID_ARG;
+  if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
+  if (scale_kind < CEK_SCALE_PERN_F16 || scale_kind > CEK_SCALE_PERT_F32) return CEK_ERR_INVALID_ARG;
+  if (flags & ~(unsigned)CEK_GEMV_EARLY_WEIGHTS) return CEK_ERR_INVALID_ARG;
+  if (!x) return CEK_ERR_INVALID_ARG;
+  int64_t total = 0;
+  for (int m = 0; m < count; ++m) {
+    if (Ns[m] <= 0 || Ns[m] > INT32_MAX || !ws[m] || !scales[m] || !ys[m]) return CEK_ERR_INVALID_ARG;
+    if (!aligned16(ws[m])) return CEK_ERR_ALIGNMENT;
+    total += Ns[m];
+  }
+  if (M == 0) return CEK_OK;
+  if (!aligned16(x)) return CEK_ERR_ALIGNMENT;
+  cek::GemvParams p = {};
+  p.x = x;
+  p.M = (int)M; p.N = (int)std::min<int64_t>(total, INT32_MAX); p.K = (int)K;
+  p.early_weights = (flags & CEK_GEMV_EARLY_WEIGHTS) ? 1 : 0;
+  p.nmat = count;
+  for (int m = 0; m < count; ++m) {
+    p.mws[m] = static_cast<const uint8_t*>(ws[m]);
+    p.mscales[m] = scales[m];
+    p.mys[m] = ys[m];
+    p.mns[m] = (int)Ns[m];
+  }
+  p.w = p.mws[0]; p.scale = p.mscales[0]; p.y = p.mys[0];
+  return cek::gemv_launch(p, x_dtype, y_dtype, w_fmt, scale_kind, false, static_cast<cudaStream_t>(stream));
 }

@@ -55,6 +55,48 @@ at::Tensor esimd_gemv_fp8_pern(at::Tensor input, at::Tensor weight, at::Tensor w
   return run_gemv("esimd_gemv_fp8_pern", input, weight, weight_scale, output, N, K, false);
 }
 
+// New op, the reference's fused multi-GEMV (fp8_GEMV_v2.h:197-316, compiled
+// there but not registered): outputs[i] = GEMV(input, weights[i], scales[i])
+// for up to 4 matrices sharing input, in one launch.
+void esimd_gemv_fp8_pern_fused(at::Tensor input, std::vector<at::Tensor> weights,
+                               std::vector<at::Tensor> weight_scales, std::vector<at::Tensor> outputs) {
+  const char* op = "esimd_gemv_fp8_pern_fused";
+  const size_t n = weights.size();
+  TORCH_CHECK(n >= 1 && n <= 4 && weight_scales.size() == n && outputs.size() == n, op,
+              ": 1 to 4 weights, with one scale and one output each");
+  check_cuda(input, op, "input");
+  TORCH_CHECK(is_half_or_bf16(input), op, ": input must be fp16 or bf16");
+  const int64_t K = weights[0].size(-1);
+  TORCH_CHECK(K > 0 && input.numel() % K == 0, op, ": input numel must be a multiple of K");
+  const int64_t M = input.numel() / K;
+  const void* wp[4];
+  const void* sp[4];
+  void* yp[4];
+  int64_t ns[4];
+  int fmt = -1, sk = -1;
+  for (size_t i = 0; i < n; ++i) {
+    check_cuda(weights[i], op, "weight");
+    check_cuda(weight_scales[i], op, "weight_scale");
+    check_cuda(outputs[i], op, "output");
+    TORCH_CHECK(weights[i].dim() == 2 && weights[i].size(1) == K, op, ": weights must be [N_i, K]");
+    TORCH_CHECK(outputs[i].scalar_type() == input.scalar_type(), op, ": outputs must match the input dtype");
+    ns[i] = weights[i].size(0);
+    TORCH_CHECK(outputs[i].numel() == M * ns[i], op, ": output i must be [M, N_i]");
+    const int f = fp8_format(weights[i], op), k = scale_kind(weight_scales[i], ns[i], true, op);
+    TORCH_CHECK((fmt < 0 || f == fmt) && (sk < 0 || k == sk), op,
+                ": all weights must share one FP8 format and one scale kind");
+    fmt = f;
+    sk = k;
+    wp[i] = weights[i].data_ptr();
+    sp[i] = weight_scales[i].data_ptr();
+    yp[i] = outputs[i].data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(input.device());
+  check_status(cek_gemv_fp8_multi(input.data_ptr(), wp, sp, yp, ns, (int)n, M, K, io_dtype(input),
+                                  io_dtype(input), fmt, sk, gemv_flags(), stream_of(input)),
+               op);
+}
+
 // Reference: esimd_gemv_fp8_pert (csrc/xpu/esimd_kernel.sycl:57-89); N, K from weight.
 at::Tensor esimd_gemv_fp8_pert(at::Tensor input, at::Tensor weight, at::Tensor weight_scale,
                                at::Tensor output) {
@@ -195,6 +237,10 @@ TORCH_LIBRARY(custom_esimd_kernels_vllm, m) {
   m.def("esimd_fused_add_rms_norm_batched(Tensor hidden_states, Tensor residual, "
         "Tensor weight, float eps) -> Tensor");
   m.impl("esimd_fused_add_rms_norm_batched", c10::DispatchKey::CUDA, &esimd_fused_add_rms_norm_batched);
+
+  m.def("esimd_gemv_fp8_pern_fused(Tensor input, Tensor[] weights, Tensor[] weight_scales, "
+        "Tensor(a!)[] outputs) -> ()");
+  m.impl("esimd_gemv_fp8_pern_fused", c10::DispatchKey::CUDA, &esimd_gemv_fp8_pern_fused);
 
   m.def("esimd_fused_add_rms_norm_batched_fp8(Tensor hidden_states, Tensor residual, "
         "Tensor weight, float eps, Tensor qweight, Tensor qweight_scale, Tensor output) -> Tensor");

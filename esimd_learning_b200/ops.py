@@ -27,6 +27,17 @@ def esimd_gemv_fp8_pern(
     return _ops.esimd_gemv_fp8_pern(input, weight, weight_scale, output, N, K)
 
 
+def esimd_gemv_fp8_pern_fused(
+    input: torch.Tensor, weights: list, weight_scales: list, outputs: list,
+) -> list:
+    """Several FP8 GEMVs that share `input`, in one launch (the reference's
+    fused multi-GEMV, fp8_GEMV_v2.h:197-316): outputs[i] = input @
+    deq(weights[i])^T * weight_scales[i], for 1 to 4 matrices with one FP8
+    format and one scale kind.  Returns outputs."""
+    _ops.esimd_gemv_fp8_pern_fused(input, weights, weight_scales, outputs)
+    return outputs
+
+
 def esimd_gemv_fp8_pert(
     input: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
     output: torch.Tensor,

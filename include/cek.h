@@ -76,6 +76,18 @@ CEK_API int cek_gemv_fp8(const void* x, const void* w, const void* scale, void* 
                          int64_t M, int64_t N, int64_t K, int x_dtype, int y_dtype,
                          int w_fmt, int scale_kind, unsigned flags, void* stream);
 
+/* ---- several FP8 GEMVs sharing one activation, one launch ---------------
+ * For m < count: ys[m][M, Ns[m]] = GEMV(x, ws[m] [Ns[m], K], scales[m]) as
+ * cek_gemv_fp8 (one scale kind and FP8 format for all).  count <= 4; the
+ * pointer arrays are HOST arrays of device pointers.  Saves the launch and
+ * ramp of each extra matrix (e.g. gate + up, qkvz + ba).
+ * Replaces: GEMV_fp8_pern_fused_host (csrc/xpu/esimd_kernels/fp8_GEMV_v2.h:262),
+ *           GEMV_fp8_pert_fused_host (csrc/xpu/esimd_kernels/fp8_GEMV_v2.h:505). */
+CEK_API int cek_gemv_fp8_multi(const void* x, const void* const* ws, const void* const* scales,
+                               void* const* ys, const int64_t* Ns, int count, int64_t M, int64_t K,
+                               int x_dtype, int y_dtype, int w_fmt, int scale_kind, unsigned flags,
+                               void* stream);
+
 /* ---- residual add + RMSNorm (batched, in place) ---------------------------
  * residual[r, :] = fp16(hidden[r, :] + residual[r, :])
  * hidden[r, :]   = fp16(f32(residual[r, :]) * rsqrt(mean((h + r)^2) + eps) * weight)

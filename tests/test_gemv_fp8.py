@@ -239,3 +239,44 @@ def test_cuda_graph_capture(ext, cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(y, ref)
 
+
+
+# reference benchmark_fused cases (tests/test_gemv_fp8.py:299-303) plus ragged ones
+MULTI_CASES = [[(3072, 2048), (16, 2048)], [(512, 2048), (512, 2048)], [(128, 2048), (128, 2048)],
+               [(100, 1024), (33, 1024), (2000, 1024), (16, 1024)]]
+
+
+@pytest.mark.parametrize("shapes", MULTI_CASES)
+@pytest.mark.parametrize("M", [1, 4, 12])
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_fused_multi_gemv(ext, cuda_device, shapes, M, io):
+    """esimd_gemv_fp8_pern_fused == the per-matrix oracle GEMVs."""
+    K = shapes[0][1]
+    torch.manual_seed(M)
+    x = (torch.randn(M, K) * 0.5).to(io)
+    ws, ss, ys = [], [], []
+    for i, (N, _) in enumerate(shapes):
+        _, wq, s = gemv_case(1, N, K, seed=100 + i)
+        ws.append(wq)
+        ss.append(s.half())  # the reference's fp16 per-N scale
+        ys.append(torch.zeros(M, N, dtype=io, device=cuda_device))
+    ext.esimd_gemv_fp8_pern_fused(x.to(cuda_device), [w.to(cuda_device) for w in ws],
+                                  [s.to(cuda_device) for s in ss], ys)
+    for wq, s, y in zip(ws, ss, ys):
+        O.assert_parity(y, O.gemv_fp8(x, wq, s), f"multi N={wq.shape[0]} M={M}")
+
+
+def test_fused_multi_gemv_cabi(cuda_device):
+    import ctypes
+    K, M = 512, 3
+    Ns = [64, 200]
+    x, _, _ = gemv_case(M, 16, K, seed=1, device=cuda_device)
+    parts = [gemv_case(1, N, K, seed=N, device=cuda_device)[1:] for N in Ns]
+    ys = [torch.zeros(M, N, dtype=torch.float16, device=cuda_device) for N in Ns]
+    P = ctypes.c_void_p * 2
+    cabi.call("cek_gemv_fp8_multi", cabi.ptr(x), P(*[cabi.ptr(w) for w, _ in parts]),
+              P(*[cabi.ptr(s) for _, s in parts]), P(*[cabi.ptr(y) for y in ys]), (ctypes.c_int64 * 2)(*Ns), 2,
+              M, K, cabi.CEK_F16, cabi.CEK_F16, cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, 0, cabi.current_stream())
+    torch.cuda.synchronize()
+    for (w, s), y in zip(parts, ys):
+        O.assert_parity(y, O.gemv_fp8(x.cpu(), w.cpu(), s.cpu()), "cabi multi")

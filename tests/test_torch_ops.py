@@ -30,6 +30,7 @@ def test_reference_schemas_are_identical(ext):
 def test_new_ops_registered(ext):
     for name in ("esimd_fused_add_rms_norm_batched_fp8", "esimd_gelu_and_mul",
                  "esimd_qkv_norm_rope", "esimd_quant_fp8_per_token", "esimd_set_weight_prefetch",
+                 "esimd_gemv_fp8_pern_fused",
                  "esimd_gemm_fp8_pertoken_pern"):
         assert hasattr(torch.ops.custom_esimd_kernels_vllm, name)
 

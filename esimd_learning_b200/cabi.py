@@ -51,6 +51,8 @@ SIGNATURES = {
     "cek_comm_errors": (_I, [_P, ctypes.POINTER(ctypes.c_uint32)]),
     "cek_gemv_fp8_allreduce": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _I64, _I, _I, _U, _P]),
     "cek_gemm_fp8_scaled": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
+    "cek_gemm_fp8w_workspace_bytes": (_I64, [_I64, _I64]),
+    "cek_gemm_fp8w": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P]),
     "cek_gemm_fp8_timeouts": (_I, [ctypes.POINTER(ctypes.c_uint64)]),
 }
 

@@ -29,25 +29,33 @@
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
+#include <type_traits>
 #include <mutex>
 
 namespace cek {
 namespace gemm {
 
-constexpr int BM = 128, BK = 128;  // BK in bytes (= e4m3 elements)
+constexpr int BM = 128, BK = 128;  // BK in bytes: 128 e4m3 or 64 fp16/bf16 elements
+
+// Operand kinds: e4m3 x e4m3 (tcgen05 kind::f8f6f4), fp16 x fp16 and
+// bf16 x bf16 (kind::f16).  All K-major, fp32 accumulation.
+enum Kind { kE4M3 = 0, kF16 = 1, kBF16 = 2 };
 constexpr int THREADS = 6 * 32;
 constexpr int TMEM_COLS = 512;     // two accumulators of up to 256 fp32 columns
 constexpr int kSmemBudget = 227 * 1024;
 
 // Tile-N dependent constants.  BN is a multiple of 32 in [128, 256]; the
 // stage count fills the shared-memory budget.
-template <int BN>
+template <int BN, int KIND>
 struct Tile {
   static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (kSmemBudget - 2048) / STAGE_BYTES > 6 ? 6 : (kSmemBudget - 2048) / STAGE_BYTES;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
-  // fp32 accumulate, A and B e4m3, both K-major, N = BN, M = 128
-  static constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+  // fp32 accumulate (bit 4), A/B format (bits 7-9 / 10-12: e4m3 = 0 for
+  // kind::f8f6f4; f16 = 0, bf16 = 1 for kind::f16), both K-major, N = BN, M = 128
+  static constexpr uint32_t FMT = KIND == kBF16 ? 1u : 0u;
+  static constexpr uint32_t IDESC =
+      (1u << 4) | (FMT << 7) | (FMT << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 };
 constexpr uint32_t kWaitPolls = 1u << 24;
 
@@ -100,11 +108,18 @@ CEK_DEVICE uint64_t smem_desc(uint32_t addr) {
   d |= (uint64_t)2 << 61;                         // 128-byte swizzle
   return d;
 }
-CEK_DEVICE void mma_f8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p; }"
-      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
+template <int KIND>
+CEK_DEVICE void mma_issue(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (KIND == kE4M3)
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p; }"
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
+  else
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
 }
 CEK_DEVICE void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -125,18 +140,22 @@ CEK_DEVICE void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 struct Params {
-  const float* a_scale;
-  const float* b_scale;
+  const float* a_scale;  // per-row [M], or null (1.0)
+  const float* b_scale;  // per-column [N], or a scalar when b_scalar
   void* y;
   int M, N, K;
   int num_m, num_n;
+  int kblocks;           // K bytes / BK
+  int kblock_elems;      // elements per k-block (TMA x step)
+  int b_scalar;
 };
 
-template <typename OutT, int BN>
+template <typename OutT, int BN, int KIND>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const Params p) {
-  constexpr int STAGES = Tile<BN>::STAGES, STAGE_BYTES = Tile<BN>::STAGE_BYTES, A_BYTES = Tile<BN>::A_BYTES;
+  using TL = Tile<BN, KIND>;
+  constexpr int STAGES = TL::STAGES, STAGE_BYTES = TL::STAGE_BYTES, A_BYTES = TL::A_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
@@ -146,7 +165,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_tiles = p.num_m * p.num_n;
-  const int kblocks = p.K / BK;
+  const int kblocks = p.kblocks;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -185,8 +204,8 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           uint8_t* sa = smem + s * STAGE_BYTES;
           const uint32_t fb = saddr(&full_bar[s]);
           bar_expect_tx(fb, STAGE_BYTES);
-          tma_load_2d(saddr(sa), &map_a, kb * BK, mb * BM, fb);
-          tma_load_2d(saddr(sa + A_BYTES), &map_b, kb * BK, nb * BN, fb);
+          tma_load_2d(saddr(sa), &map_a, kb * p.kblock_elems, mb * BM, fb);
+          tma_load_2d(saddr(sa + A_BYTES), &map_b, kb * p.kblock_elems, nb * BN, fb);
         }
       }
       // Before leaving, make sure no copy of ours is still landing (bounded).
@@ -210,7 +229,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           const uint32_t a0 = saddr(smem + s * STAGE_BYTES), b0 = a0 + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k)
-            mma_f8(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), Tile<BN>::IDESC, (kb | k) ? 1u : 0u);
+            mma_issue<KIND>(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), TL::IDESC, (kb | k) ? 1u : 0u);
           mma_commit(saddr(&empty_bar[s]));
         }
         if (!ok) break;
@@ -233,7 +252,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       fence_after();
       const int row = mb * BM + quad * 32 + lane;
       const bool rv = row < p.M;
-      const float as = rv ? p.a_scale[row] : 0.f;
+      const float as = rv ? (p.a_scale ? p.a_scale[row] : 1.f) : 0.f;
       OutT* yrow = y + (size_t)(rv ? row : 0) * p.N;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + b * 256;
 #pragma unroll 1
@@ -249,7 +268,8 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           for (int i = 0; i < 16; ++i) {
             const int n = n0 + 2 * i;
             const bool nv = i < 8 || hi;
-            const float bs0 = nv ? __ldg(p.b_scale + n) : 0.f, bs1 = nv ? __ldg(p.b_scale + n + 1) : 0.f;
+            const float bs0 = nv ? __ldg(p.b_scale + (p.b_scalar ? 0 : n)) : 0.f;
+            const float bs1 = nv ? __ldg(p.b_scale + (p.b_scalar ? 0 : n + 1)) : 0.f;
             o[i] = pack2<OutT>(__uint_as_float(r[2 * i]) * as * bs0,
                                __uint_as_float(r[2 * i + 1]) * as * bs1);
           }
@@ -290,23 +310,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows) {
-  // box_rows <= 256 (TMA box limit); BN and BM are both within it
+// Row-major [rows, cols] matrix of `eb`-byte elements; box = one 128-byte
+// k-block x box_rows rows (box_rows <= 256, the TMA box limit).
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int eb = 1) {
   auto enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * eb)};
+  cuuint32_t box[2] = {(cuuint32_t)(BK / eb), (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+  return enc(m, eb == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename OutT, int BN>
+template <typename OutT, int BN, int KIND>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t st) {
-  auto kern = gemm_fp8_kernel<OutT, BN>;
-  constexpr int SMEM_BYTES = Tile<BN>::SMEM_BYTES;
+  auto kern = gemm_fp8_kernel<OutT, BN, KIND>;
+  constexpr int SMEM_BYTES = Tile<BN, KIND>::SMEM_BYTES;
   static unsigned attr_set = 0;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -331,21 +352,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaSt
   return cudaLaunchKernelEx(&cfg, kern, ma, mb, p) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
 }
 
-}  // namespace gemm
-}  // namespace cek
-
-extern "C" int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* a_scale,
-                                   const float* b_scale, void* y, int64_t M, int64_t N, int64_t K,
-                                   int y_dtype, void* stream) {
-  using namespace cek::gemm;
-  if (M < 0 || N < 0 || K < 0) return CEK_ERR_INVALID_ARG;
-  if (y_dtype != CEK_F16 && y_dtype != CEK_BF16) return CEK_ERR_INVALID_ARG;
-  if (M == 0 || N == 0) return CEK_OK;
-  if (K == 0 || K % BK != 0 || N % 16 != 0) return CEK_ERR_INVALID_ARG;
-  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return CEK_ERR_INVALID_ARG;
-  if (!aq || !bq || !a_scale || !b_scale || !y) return CEK_ERR_INVALID_ARG;
-  if (!cek_host::aligned16(aq) || !cek_host::aligned16(bq) || !cek_host::aligned16(y))
-    return CEK_ERR_ALIGNMENT;
+int choose_bn(int64_t M, int64_t N) {
   // Tile N: the candidate that minimises (rounds of tiles over the SMs) x BN,
   // i.e. the persistent grid's critical path.  A narrower tile must win by
   // more than 3 %: per FLOP it is slightly slower (measured: at M = 8192,
@@ -367,20 +374,111 @@ extern "C" int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* 
     return v ? std::atoi(v) : 0;
   }();
   if (bn_env == 256 || bn_env == 224 || bn_env == 192 || bn_env == 160) bn = bn_env;
+  return bn;
+}
+
+// Builds the maps and launches: a [M, K] and b [N, K], elements of `eb` bytes.
+template <int KIND>
+int run(const void* a, const void* b, const float* a_scale, const float* b_scale, bool b_scalar, void* y,
+        int64_t M, int64_t N, int64_t K, int eb, int y_dtype, cudaStream_t st) {
+  const int bn = choose_bn(M, N);
   CUtensorMap ma, mb;
-  if (!make_map(&ma, aq, M, K, BM) || !make_map(&mb, bq, N, K, bn)) return CEK_ERR_LAUNCH;
+  if (!make_map(&ma, a, M, K, BM, eb) || !make_map(&mb, b, N, K, bn, eb)) return CEK_ERR_LAUNCH;
   Params p;
   p.a_scale = a_scale; p.b_scale = b_scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
-  p.num_m = (int)num_m;
+  p.num_m = (int)((M + BM - 1) / BM);
   p.num_n = (int)((N + bn - 1) / bn);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  p.kblocks = (int)(K * eb / BK);
+  p.kblock_elems = BK / eb;
+  p.b_scalar = b_scalar ? 1 : 0;
 #define CEK_GEMM_BN(B)                                                                        \
-  if (bn == B) return y_dtype == CEK_F16 ? launch<__half, B>(ma, mb, p, st)                  \
-                                         : launch<__nv_bfloat16, B>(ma, mb, p, st);
+  if (bn == B) return y_dtype == CEK_F16 ? launch<__half, B, KIND>(ma, mb, p, st)            \
+                                         : launch<__nv_bfloat16, B, KIND>(ma, mb, p, st);
   CEK_GEMM_BN(256) CEK_GEMM_BN(224) CEK_GEMM_BN(192) CEK_GEMM_BN(160)
 #undef CEK_GEMM_BN
   return CEK_ERR_UNSUPPORTED;
+}
+
+// Exact FP8 -> 16-bit dequantisation of a weight matrix (8 codes per thread).
+template <typename T, int FMT>
+__global__ void __launch_bounds__(256) dequant_fp8_kernel(const uint8_t* __restrict__ w, T* __restrict__ out,
+                                                          int64_t n8) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const uint2 v = reinterpret_cast<const uint2*>(w)[i];
+  uint32_t o[4];
+  const uint32_t words[2] = {v.x, v.y};
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    if constexpr (std::is_same<T, __half>::value) {
+      o[2 * q] = fp8x2_to_f16x2<FMT>(words[q] & 0xFFFFu);
+      o[2 * q + 1] = fp8x2_to_f16x2<FMT>(words[q] >> 16);
+    } else {
+      o[2 * q] = fp8x2_to_bf16x2<FMT>(words[q] & 0xFFFFu);
+      o[2 * q + 1] = fp8x2_to_bf16x2<FMT>(words[q] >> 16);
+    }
+  }
+  reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+}  // namespace gemm
+}  // namespace cek
+
+extern "C" int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* a_scale,
+                                   const float* b_scale, void* y, int64_t M, int64_t N, int64_t K,
+                                   int y_dtype, void* stream) {
+  using namespace cek::gemm;
+  if (M < 0 || N < 0 || K < 0) return CEK_ERR_INVALID_ARG;
+  if (y_dtype != CEK_F16 && y_dtype != CEK_BF16) return CEK_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return CEK_OK;
+  if (K == 0 || K % BK != 0 || N % 16 != 0) return CEK_ERR_INVALID_ARG;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return CEK_ERR_INVALID_ARG;
+  if (!aq || !bq || !a_scale || !b_scale || !y) return CEK_ERR_INVALID_ARG;
+  if (!cek_host::aligned16(aq) || !cek_host::aligned16(bq) || !cek_host::aligned16(y))
+    return CEK_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return cek::gemm::run<cek::gemm::kE4M3>(aq, bq, a_scale, b_scale, false, y, M, N, K, 1, y_dtype, st);
+}
+
+extern "C" int64_t cek_gemm_fp8w_workspace_bytes(int64_t N, int64_t K) {
+  if (N <= 0 || K <= 0) return 0;
+  return ((N * K * 2 + 255) / 256) * 256;
+}
+
+extern "C" int cek_gemm_fp8w(const void* x, const void* w, const void* scale, void* y, void* workspace,
+                             int64_t workspace_bytes, int64_t M, int64_t N, int64_t K, int dtype, int w_fmt,
+                             int scale_kind, void* stream) {
+  using namespace cek::gemm;
+  if (M < 0 || N < 0 || K < 0 || workspace_bytes < 0) return CEK_ERR_INVALID_ARG;
+  if (dtype != CEK_F16 && dtype != CEK_BF16) return CEK_ERR_INVALID_ARG;
+  if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
+  if (scale_kind != CEK_SCALE_PERN_F32 && scale_kind != CEK_SCALE_PERT_F32) return CEK_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return CEK_OK;
+  if (K == 0 || K % 64 != 0 || N % 16 != 0) return CEK_ERR_INVALID_ARG;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return CEK_ERR_INVALID_ARG;
+  if (!x || !w || !scale || !y || !workspace) return CEK_ERR_INVALID_ARG;
+  if (workspace_bytes < cek_gemm_fp8w_workspace_bytes(N, K)) return CEK_ERR_INVALID_ARG;
+  if (!cek_host::aligned16(x) || !cek_host::aligned16(w) || !cek_host::aligned16(y) ||
+      !cek_host::aligned16(workspace))
+    return CEK_ERR_ALIGNMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t n8 = N * K / 8;
+  const unsigned blocks = (unsigned)((n8 + 255) / 256);
+  const uint8_t* wq = static_cast<const uint8_t*>(w);
+#define CEK_DQ(T, F) cek::gemm::dequant_fp8_kernel<T, F><<<blocks, 256, 0, st>>>(wq, static_cast<T*>(workspace), n8)
+  if (dtype == CEK_F16) {
+    if (w_fmt == CEK_E4M3) CEK_DQ(__half, CEK_E4M3); else CEK_DQ(__half, CEK_E5M2);
+  } else {
+    if (w_fmt == CEK_E4M3) CEK_DQ(__nv_bfloat16, CEK_E4M3); else CEK_DQ(__nv_bfloat16, CEK_E5M2);
+  }
+#undef CEK_DQ
+  if (cudaGetLastError() != cudaSuccess) return CEK_ERR_LAUNCH;
+  const float* sc = static_cast<const float*>(scale);
+  const bool scalar = scale_kind == CEK_SCALE_PERT_F32;
+  return dtype == CEK_F16
+             ? run<kF16>(x, workspace, nullptr, sc, scalar, y, M, N, K, 2, dtype, st)
+             : run<kBF16>(x, workspace, nullptr, sc, scalar, y, M, N, K, 2, dtype, st);
 }
 
 extern "C" int cek_gemm_fp8_timeouts(uint64_t* count) {

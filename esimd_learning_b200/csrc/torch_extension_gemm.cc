@@ -9,9 +9,16 @@ using namespace cek_torch;
 
 // Reference: esimd_gemm_fp8_pert (csrc/xpu/esimd_kernel_gemm.sycl:23-64).
 // bf16 I/O runs natively (the reference converts through fp16 copies,
-// esimd_kernel_gemm.sycl:45-48,61-63).  Every M runs the tensor-core GEMV
-// family: one weight pass per 16-token tile, the tiles of one row group
-// scheduled next to each other so re-reads hit L2.
+// esimd_kernel_gemm.sycl:45-48,61-63).  Decode sizes (M <= 64) run the
+// tensor-core GEMV family: one weight pass per 16-token tile, the tiles of
+// one row group scheduled next to each other so re-reads hit L2.  Prefill
+// sizes (M > 64, K % 64 == 0, N % 16 == 0) dequantise the weight exactly into
+// a 16-bit workspace and run the tcgen05 GEMM (cek_gemm_fp8w).
+// Token count above which the per-tensor GEMM leaves the GEMV family for the
+// tcgen05 GEMM (the reference's own decode/prefill split,
+// csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4043-4048).
+constexpr int64_t kGemmMinRows = 64;
+
 at::Tensor esimd_gemm_fp8_pert(at::Tensor input, at::Tensor weight, at::Tensor weight_scale,
                                at::Tensor output) {
   const char* op = "esimd_gemm_fp8_pert";
@@ -32,6 +39,16 @@ at::Tensor esimd_gemm_fp8_pert(at::Tensor input, at::Tensor weight, at::Tensor w
   TORCH_CHECK(output.numel() == M * N, op, ": output must be [M, N]");
   const int fmt = fp8_format(weight, op);
   c10::cuda::CUDAGuard guard(input.device());
+  if (M > kGemmMinRows && K % 64 == 0 && N % 16 == 0 && input.is_contiguous() && output.is_contiguous() &&
+      weight.is_contiguous()) {
+    const int64_t ws_bytes = cek_gemm_fp8w_workspace_bytes(N, K);
+    at::Tensor ws = at::empty({ws_bytes}, input.options().dtype(at::kByte));
+    check_status(cek_gemm_fp8w(input.data_ptr(), weight.data_ptr(), weight_scale.data_ptr(), output.data_ptr(),
+                               ws.data_ptr(), ws_bytes, M, N, K, io_dtype(input), fmt, CEK_SCALE_PERT_F32,
+                               stream_of(input)),
+                 op);
+    return output;
+  }
   check_status(cek_gemv_fp8(input.data_ptr(), weight.data_ptr(), weight_scale.data_ptr(),
                             output.data_ptr(), M, N, K, io_dtype(input), io_dtype(output), fmt,
                             CEK_SCALE_PERT_F32, gemv_flags(), stream_of(input)),

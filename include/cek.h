@@ -217,6 +217,22 @@ CEK_API int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* a_s
                                 const float* b_scale, void* y, int64_t M, int64_t N,
                                 int64_t K, int y_dtype, void* stream);
 
+/* FP8-weight GEMM with 16-bit activations on the tcgen05 tensor cores:
+ *   y[m, n] = T( sum_k x[m, k] * deq(w[n, k]) * scale )
+ * Replaces the prefill branch of the reference's esimd_gemm_fp8_pert
+ * (csrc/xpu/esimd_kernel_gemm.sycl:23-64 -> GEMM_fp8_pert_dispatch,
+ * csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4043-4048, M > 64).
+ * w is first dequantised exactly (every e4m3/e5m2 value is a 16-bit float
+ * of dtype) into `workspace` (cek_gemm_fp8w_workspace_bytes(N, K) bytes),
+ * then one kind::f16 tcgen05 GEMM with fp32 accumulation runs; the scale
+ * (fp32 per-tensor scalar, or fp32 per-N) is applied in the epilogue.
+ * x, y, T = dtype (CEK_F16 / CEK_BF16), row-major and contiguous.
+ * K % 64 == 0 and N % 16 == 0; x, w, y, workspace 16-byte aligned. */
+CEK_API int64_t cek_gemm_fp8w_workspace_bytes(int64_t N, int64_t K);
+CEK_API int cek_gemm_fp8w(const void* x, const void* w, const void* scale, void* y,
+                          void* workspace, int64_t workspace_bytes, int64_t M, int64_t N,
+                          int64_t K, int dtype, int w_fmt, int scale_kind, void* stream);
+
 /* Number of bounded device waits in cek_gemm_fp8_scaled kernels that gave up
  * since the library was loaded (0 in a healthy run).  Synchronous. */
 CEK_API int cek_gemm_fp8_timeouts(uint64_t* count);

@@ -3,6 +3,9 @@
 * esimd_gemm_fp8_pert (the reference op): the reference's
   tests/test_gemm_fp8.py shapes, M in {1..64}, fp16/bf16 I/O, e4m3/e5m2
   weights, and GEMM(M=1) == GEMV (tests/test_gemm_fp8.py:65-93).
+* esimd_gemm_fp8_pert at prefill sizes (M > 64): the weight dequantised to
+  fp16/bf16, then the kind::f16 tcgen05 GEMM; ragged M, N tails, and the C ABI
+  with a per-N scale.
 * the tcgen05 prefill GEMM (per-token x per-channel scales)
   shapes and ragged M / N edges, against the fp32 oracle of the same
   quantised operands; quantisation itself is bit-exact (test_elementwise).
@@ -33,6 +36,61 @@ def test_gemm_pert_correctness(ext, cuda_device, N, K, wdt, io):
         ext.esimd_gemm_fp8_pert(x.to(cuda_device), w.to(cuda_device),
                                 torch.tensor(sv, dtype=torch.float32, device=cuda_device), out)
         O.assert_parity(out, O.gemv_fp8(x, w, torch.tensor(sv)), f"M={M} N={N} K={K} {wdt} {io}")
+
+
+@pytest.mark.parametrize("M,N,K", [(65, 256, 512), (128, 512, 256), (300, 1040, 384), (257, 2048, 2048),
+                                   (1000, 4096, 1024)])
+@pytest.mark.parametrize("wdt", [torch.float8_e4m3fn, torch.float8_e5m2])
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_gemm_pert_prefill(ext, cuda_device, M, N, K, wdt, io):
+    torch.manual_seed(1)
+    w = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(wdt)
+    sv = 0.05 + torch.rand(1).item() * 0.1
+    x = (torch.randn(M, K) * 0.1).to(io)
+    out = torch.full((M, N), float("nan"), dtype=io, device=cuda_device)
+    ext.esimd_gemm_fp8_pert(x.to(cuda_device), w.to(cuda_device),
+                            torch.tensor(sv, dtype=torch.float32, device=cuda_device), out)
+    O.assert_parity(out, O.gemv_fp8(x, w, torch.tensor(sv)), f"M={M} N={N} K={K} {wdt} {io}")
+
+
+def test_gemm_pert_prefill_config3(ext, cuda_device):
+    """fp16 activations [2048, 4096] x e4m3 [14336, 4096], per-tensor scale;
+    the oracle checks a strided sample of rows."""
+    M, N, K = 2048, 14336, 4096
+    torch.manual_seed(2)
+    w = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(torch.float8_e4m3fn)
+    x = (torch.randn(M, K) * 0.1).half()
+    s = torch.tensor(0.07, dtype=torch.float32)
+    out = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda_device)
+    ext.esimd_gemm_fp8_pert(x.to(cuda_device), w.to(cuda_device), s.to(cuda_device), out)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    rows = torch.arange(0, M, 67)
+    O.assert_parity(out.cpu()[rows], O.gemv_fp8(x[rows], w, s), "pert prefill config3")
+
+
+def test_gemm_fp8w_cabi_pern(cuda_device):
+    """C ABI with a per-N fp32 scale, bf16 I/O; workspace size rule and shape checks."""
+    M, N, K = 200, 272, 320
+    torch.manual_seed(3)
+    w = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(torch.float8_e4m3fn)
+    sc = torch.rand(N) * 0.1 + 0.01
+    x = (torch.randn(M, K) * 0.1).bfloat16()
+    L = cabi.lib()
+    nb = L.cek_gemm_fp8w_workspace_bytes(N, K)
+    assert nb >= N * K * 2 and nb % 256 == 0
+    ws = torch.empty(nb, dtype=torch.uint8, device=cuda_device)
+    wd, sd, xd = w.to(cuda_device), sc.to(cuda_device), x.to(cuda_device)
+    y = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda_device)
+    cabi.call("cek_gemm_fp8w", cabi.ptr(xd), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(y), cabi.ptr(ws), nb,
+              M, N, K, cabi.CEK_BF16, cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, cabi.current_stream())
+    torch.cuda.synchronize()
+    O.assert_parity(y, O.gemv_fp8(x, w, sc), "fp8w cabi pern")
+    args = (cabi.ptr(xd), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(y), cabi.ptr(ws))
+    assert L.cek_gemm_fp8w(*args, nb - 256, M, N, K, cabi.CEK_BF16, cabi.CEK_E4M3,
+                           cabi.CEK_SCALE_PERN_F32, None) == cabi.CEK_ERR_INVALID_ARG
+    assert L.cek_gemm_fp8w(*args, nb, M, N, 96, cabi.CEK_BF16, cabi.CEK_E4M3,
+                           cabi.CEK_SCALE_PERN_F32, None) == cabi.CEK_ERR_INVALID_ARG
 
 
 def test_gemm_vs_gemv_m1(ext, cuda_device):

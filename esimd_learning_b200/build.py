@@ -30,7 +30,7 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-CU_SOURCES = ["abi.cu", "gemv_fp8.cu", "rmsnorm.cu", "elementwise.cu", "tp_allreduce.cu", "gemm_fp8_tcgen05.cu"]
+CU_SOURCES = ["abi.cu", "gemv_fp8.cu", "gemv_fp8_bulk.cu", "rmsnorm.cu", "elementwise.cu", "tp_allreduce.cu", "gemm_fp8_tcgen05.cu"]
 EXT_MODULES = {
     "custom_esimd_kernels": "torch_extension.cc",
     "custom_esimd_kernels_gemm": "torch_extension_gemm.cc",

@@ -41,15 +41,18 @@ CEK_DEVICE uint4 ldg_nc(const void* p) {
 // `pair` holds two FP8 codes in its low 16 bits (byte 0 -> low half of the
 // result, byte 1 -> high half), matching the mma.sync fragment convention that
 // the lower 16 bits carry the lower k index.
-template <int FMT>
+template <int FMT, int HI = 0>
 CEK_DEVICE uint32_t fp8x2_to_f16x2(uint32_t pair) {
+  // HI = 1 converts bytes 2 and 3 of `pair` instead of bytes 0 and 1.
   uint32_t r;
   if constexpr (FMT == CEK_E4M3) {
-    asm("{ .reg .b16 lo; mov.b32 {lo, _}, %1; cvt.rn.f16x2.e4m3x2 %0, lo; }"
-        : "=r"(r) : "r"(pair));
+    if constexpr (HI)
+      asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %1; cvt.rn.f16x2.e4m3x2 %0, hi; }" : "=r"(r) : "r"(pair));
+    else
+      asm("{ .reg .b16 lo; mov.b32 {lo, _}, %1; cvt.rn.f16x2.e4m3x2 %0, lo; }" : "=r"(r) : "r"(pair));
   } else {
     // e5m2 is the top byte of an fp16: place each byte in the high half of its lane.
-    r = __byte_perm(pair, 0u, 0x1404);
+    r = __byte_perm(pair, 0u, HI ? 0x3424 : 0x1404);
   }
   return r;
 }
@@ -59,9 +62,9 @@ CEK_DEVICE uint32_t fp8x2_to_f16x2(uint32_t pair) {
 // the FP8 value times 2^-(127 - bias); one exact bf16x2 multiply by
 // 2^(127 - bias) restores it.  FP8 subnormals land on bf16 subnormals, which
 // the multiply handles exactly (bf16 arithmetic on sm_90+ keeps subnormals).
-template <int FMT>
+template <int FMT, int HI = 0>
 CEK_DEVICE uint32_t fp8x2_to_bf16x2(uint32_t pair) {
-  uint32_t v = __byte_perm(pair, 0u, 0x4140);  // [b0, 0, b1, 0]
+  uint32_t v = __byte_perm(pair, 0u, HI ? 0x4342 : 0x4140);  // [b0, 0, b1, 0] (HI: bytes 2, 3)
   uint32_t r;
   if constexpr (FMT == CEK_E4M3) {
     r = ((v & 0x007F007Fu) << 4) | ((v & 0x00800080u) << 8);

@@ -83,10 +83,10 @@ CEK_DEVICE void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], u
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-template <typename InT, int FMT>
+template <typename InT, int FMT, int HI = 0>
 CEK_DEVICE uint32_t cvt_pair(uint32_t pair) {
-  if constexpr (std::is_same<InT, __half>::value) return fp8x2_to_f16x2<FMT>(pair);
-  else return fp8x2_to_bf16x2<FMT>(pair);
+  if constexpr (std::is_same<InT, __half>::value) return fp8x2_to_f16x2<FMT, HI>(pair);
+  else return fp8x2_to_bf16x2<FMT, HI>(pair);
 }
 
 template <int SCALE>
@@ -123,7 +123,13 @@ CEK_DEVICE void load_x16(const GemvParams& p, int tok, int k, uint32_t (&xw)[8])
   }
 }
 
-// In-CTA split-K GEMV (any M, no scratch), launched with PDL on `st`.
+// Bulk-copy GEMV for up to 8 tokens (gemv_fp8_bulk.cu); CEK_ERR_UNSUPPORTED
+// when the call does not fit it.
+int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, int scale_kind, cudaStream_t st);
+
+// Plain calls go to gemv_bulk_launch when it accepts them; otherwise (and
+// for the fused, multi-matrix and all-reduce variants) the in-CTA split-K
+// GEMV (any M, no scratch), launched with PDL on `st`.
 int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
                 bool fused, cudaStream_t st);
 

@@ -41,7 +41,30 @@ constexpr int kMaxWarps = 16; // warps per CTA: max(8, ks)
 
 // Chunks per batch (two batches in flight per warp): 2 for one token tile,
 // 1 for two (their activation registers double).
-template <int NT> struct UnrollOf { static constexpr int value = NT == 1 ? 2 : 1; };
+#ifndef CEK_GEMV_U1
+#define CEK_GEMV_U1 2
+#endif
+template <int NT> struct UnrollOf { static constexpr int value = NT == 1 ? CEK_GEMV_U1 : 1; };
+
+// Weight stream load (16 B, read once: no L1 allocation).
+CEK_DEVICE uint4 ldg_w(const void* p) {
+  uint4 r;
+#if CEK_GEMV_WLOAD == 1
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+#elif CEK_GEMV_WLOAD == 2
+  asm volatile("ld.global.nc.L1::no_allocate.L2::128B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+#elif CEK_GEMV_WLOAD == 3
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(pol));
+#else
+  r = ldg_stream(p);
+#endif
+  return r;
+}
 
 // One batch: U chunks of 16 rows x 64 k of W for this warp's lanes, plus the
 // matching activations of the warp's NT token tiles.
@@ -66,8 +89,8 @@ CEK_DEVICE void issue_w(const GemvParams& p, const WarpCtx<NT>& c, int ch, Batch
   for (int u = 0; u < Batch<NT>::U; ++u) {
     const int kk = (ch + u) * kChunkK + c.t * 16;
     const bool ok = (ch + u < c.cend) && kk < p.K;
-    b.wa[u] = (ok && c.v0) ? ldg_stream(c.w0 + (size_t)(ch + u) * kChunkK) : make_uint4(0, 0, 0, 0);
-    b.wb[u] = (ok && c.v1) ? ldg_stream(c.w1 + (size_t)(ch + u) * kChunkK) : make_uint4(0, 0, 0, 0);
+    b.wa[u] = (ok && c.v0) ? ldg_w(c.w0 + (size_t)(ch + u) * kChunkK) : make_uint4(0, 0, 0, 0);
+    b.wb[u] = (ok && c.v1) ? ldg_w(c.w1 + (size_t)(ch + u) * kChunkK) : make_uint4(0, 0, 0, 0);
   }
 }
 
@@ -283,6 +306,10 @@ static int dispatch_fmt_scale(const GemvParams& p, const GemvLaunch& L, int w_fm
 
 int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
                 bool fused, cudaStream_t st) {
+  if (!fused && base.nmat == 0 && base.ar_world == 0) {
+    const int s = gemv_bulk_launch(base, x_dtype, y_dtype, w_fmt, scale_kind, st);
+    if (s != CEK_ERR_UNSUPPORTED) return s;
+  }
   GemvLaunch L = plan_gemv(base.M, base.N, base.K);  // multi-GEMV: N = sum of the matrices' N
   GemvParams p = base;
   p.ks = L.ks; p.rg_per_cta = L.rg_per_cta; p.mtiles = L.mtiles; p.cpw = L.cpw;

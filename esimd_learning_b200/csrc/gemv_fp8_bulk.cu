@@ -1,0 +1,323 @@
+// gemv_fp8_bulk.cu — the decode GEMV (M <= 8) as a bulk-copy stream.
+//
+//   y[m, n] = OutT( sum_k x[m, k] * deq(w[n, k]) * scale(n) )
+//
+// Same contract as the split-K kernel in gemv_fp8.cu (the reference's
+// GEMV_fp8_pern_kernel / GEMV_fp8_pert_kernel, csrc/xpu/esimd_kernels/
+// fp8_GEMV_v2.h:44-90, 322-368); this is the path for up to 8 tokens when x
+// and a few weight slabs fit in shared memory (8 * K bytes per slab).
+//
+// Why a second kernel.  With register-held weights every warp spends the
+// FP8 conversion and MMA time of a batch before it reissues that batch's
+// loads, so the bytes in flight per SM drop below what HBM needs, and each
+// warp walks 16 rows 4 KB apart, which costs DRAM row locality.  Measured on
+// gate_up (28672 x 4096): loads alone 18.9 us, with the math 24-26 us.  Here
+// the weight stream is decoupled from the math:
+//  * Persistent grid, one CTA per SM (grid = min(SMs, N / 8)).  CTA c owns
+//    the contiguous rows [N c / G, N (c + 1) / G): every CTA streams the same
+//    byte count to within one row, with no cross-CTA reduction, because a
+//    row's output needs only that row.
+//  * Warp 0, one lane: producer.  Consecutive rows are contiguous in memory,
+//    so a slab of 8 rows x K is one contiguous range; it is fetched with 1-D
+//    cp.async.bulk copies of up to 8 KB into a ring of slabs in shared memory
+//    (completion by transaction-count mbarriers; no multicast).  x [M, K] is
+//    copied once per CTA.
+//  * Warps 1-8: consumers.  Slab rows are the n = 8 columns of an
+//    mma.sync m16n8k16 (tokens are the 16 A rows, M <= 8 of them used); each
+//    consumer takes every 8th 64-k chunk of the slab, converts its FP8 bytes
+//    exactly to f16x2 / bf16x2 and accumulates in fp32.  The stage is handed
+//    back right after its last shared-memory read; the 8 partial sums of a
+//    slab are reduced through shared memory in a fixed order (deterministic
+//    results), scaled, converted and stored.
+//  * K permutation: lane (g, t) reads 16 contiguous bytes of slab row g at
+//    k = 64c + 16t and the 16 matching activations; word q feeds MMA step q
+//    (k labels 2t, 2t+1, 2t+8, 2t+9).  Any k bijection shared by both
+//    operands leaves the sum unchanged.
+//  * PDL: griddepcontrol.launch_dependents at CTA start; x is copied after
+//    griddepcontrol.wait; with `early_weights` the first slabs are requested
+//    before the wait.
+//  * Every mbarrier wait is bounded.  A wait that gives up is counted
+//    (cek_gemv_fp8_timeouts); the CTA stops waiting but keeps its barrier
+//    sequence, so it always exits.
+#include "gemv.cuh"
+#include "mbarrier.cuh"
+
+#include <algorithm>
+
+namespace cek {
+namespace bulk {
+
+#ifndef CEK_BULK_CONSUMERS
+#define CEK_BULK_CONSUMERS 8
+#endif
+#ifndef CEK_BULK_NACC
+#define CEK_BULK_NACC 2
+#endif
+constexpr int kConsumers = CEK_BULK_CONSUMERS;
+constexpr int kAcc = CEK_BULK_NACC;  // independent accumulators (shorter MMA dependency chains)
+constexpr int kThreads = 32 * (1 + kConsumers);
+constexpr int kSlabRows = 16;
+constexpr int kMaxStages = 8;
+constexpr uint32_t kPiece = 8192;          // bytes per bulk copy
+constexpr int kSmemBudget = 216 * 1024;    // dynamic shared memory per CTA (static: ~4.2 KB)
+constexpr uint32_t kWaitPolls = 1u << 22;
+
+__device__ unsigned long long g_timeouts;
+
+// x_bytes: x staged in shared memory; ks: bytes of a row per slab (K / pieces);
+// slab_bytes = 16 * ks.
+struct Plan { int x_bytes, ks, pieces, slab_bytes, stages, smem, grid; };
+
+template <typename InT, int FMT, int SCALE, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+gemv_bulk_kernel(const GemvParams p, const Plan pl) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], xbar;
+  __shared__ float red[2][kConsumers][16][8];  // [row block parity][consumer][row][token]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = p.K, KS = pl.ks, P = pl.pieces;
+  const int r0 = (int)((int64_t)p.N * blockIdx.x / gridDim.x);
+  const int r1 = (int)((int64_t)p.N * (blockIdx.x + 1) / gridDim.x);
+  const int nblocks = (r1 - r0 + kSlabRows - 1) / kSlabRows;
+  const int nslabs = nblocks * P;  // slab i = row block i / P, K piece i % P
+  const int stages = pl.stages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar::init(mbar::saddr(&full[s]), 1);
+      mbar::init(mbar::saddr(&empty[s]), kConsumers);
+    }
+    mbar::init(mbar::saddr(&xbar), 1);
+    mbar::fence_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // Producer warp.  A whole-row slab (P == 1) is one contiguous range,
+    // copied by lane 0 in kPiece parts; a K piece of 16 rows is 16 row
+    // segments, one copy per lane.
+    const uint32_t ring = mbar::saddr(smem + pl.x_bytes);
+    bool ok = true;
+    auto issue = [&](int i) {
+      const int s = i % stages, rb = i / P, pc = i - rb * P;
+      const int row0 = r0 + rb * kSlabRows;
+      const int rows = min(kSlabRows, r1 - row0);
+      const uint32_t dst = ring + (uint32_t)s * pl.slab_bytes;
+      const uint32_t bar = mbar::saddr(&full[s]);
+      if (lane == 0) mbar::arrive_expect_tx(bar, (uint32_t)rows * (uint32_t)KS);
+      __syncwarp();
+      if (P == 1) {
+        if (lane == 0) {
+          const uint8_t* src = p.w + (size_t)row0 * K;
+          const uint32_t bytes = (uint32_t)rows * (uint32_t)K;
+          for (uint32_t off = 0; off < bytes; off += kPiece)
+            mbar::bulk_g2s(dst + off, src + off, min(kPiece, bytes - off), bar);
+        }
+      } else if (lane < rows) {
+        mbar::bulk_g2s(dst + (uint32_t)lane * KS, p.w + (size_t)(row0 + lane) * K + (size_t)pc * KS, (uint32_t)KS,
+                       bar);
+      }
+    };
+    const int pre = min(stages, nslabs);
+    if (p.early_weights)
+      for (int i = 0; i < pre; ++i) issue(i);
+    pdl_wait();
+    if (lane == 0) {
+      const uint32_t xb = (uint32_t)p.M * (uint32_t)K * 2u;
+      const uint32_t bar = mbar::saddr(&xbar);
+      mbar::arrive_expect_tx(bar, xb);
+      const uint8_t* xs = static_cast<const uint8_t*>(p.x);
+      for (uint32_t off = 0; off < xb; off += kPiece)
+        mbar::bulk_g2s(mbar::saddr(smem) + off, xs + off, min(kPiece, xb - off), bar);
+    }
+    if (!p.early_weights)
+      for (int i = 0; i < pre; ++i) issue(i);
+    for (int i = pre; i < nslabs && ok; ++i) {
+      // stage i % stages is free once the consumers released use (i / stages) - 1
+      if (lane == 0) ok = mbar::wait(mbar::saddr(&empty[i % stages]), ((i / stages) + 1) & 1, kWaitPolls);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicAdd(&g_timeouts, 1ull);
+        break;  // the consumers' waits run out too
+      }
+      issue(i);
+    }
+    return;
+  }
+
+  // ---- consumers ----
+  const int cw = warp - 1, g = lane >> 2, t = lane & 3;
+  const int ctid = threadIdx.x - 32;
+  // Tokens >= M read token 0's activations: their output columns are never stored.
+  const uint32_t xrow = mbar::saddr(smem) + (uint32_t)(g < p.M ? g : 0) * K * 2u + 32u * t;
+  const int nchunks = KS / 64;
+  bool dead = !mbar::wait(mbar::saddr(&xbar), 0, kWaitPolls);
+  if (dead && lane == 0) atomicAdd(&g_timeouts, 1ull);
+
+  float acc[kAcc][4];
+  float out_scale = 0.f;
+  int out_row = 0;
+  for (int i = 0; i < nslabs; ++i) {
+    const int s = i % stages, rb = i / P, pc = i - rb * P;
+    if (pc == 0) {
+      // new row block: clear the sums; the epilogue thread fetches its scale
+      // now, so the load's latency hides behind the block's math
+#pragma unroll
+      for (int a = 0; a < kAcc; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.f;
+      out_row = r0 + rb * kSlabRows + (ctid & 15);
+      out_scale = (ctid < 16 * 8 && out_row < r1) ? load_scale<SCALE>(p.scale, out_row) : 0.f;
+    }
+    if (!dead && !mbar::wait(mbar::saddr(&full[s]), (i / stages) & 1, kWaitPolls)) {
+      dead = true;
+      if (lane == 0) atomicAdd(&g_timeouts, 1ull);
+    }
+    const uint32_t wrow = mbar::saddr(smem + pl.x_bytes) + (uint32_t)s * pl.slab_bytes + (uint32_t)g * KS + 16u * t;
+    const uint32_t wrow8 = wrow + 8u * KS;
+    const uint32_t xpc = xrow + (uint32_t)pc * KS * 2u;
+    if (!dead) {
+#pragma unroll 2
+      for (int c = cw; c < nchunks; c += kConsumers) {
+        const uint4 wa = mbar::lds16(wrow + 64u * c), wb = mbar::lds16(wrow8 + 64u * c);
+        const uint4 xa = mbar::lds16(xpc + 128u * c), xb = mbar::lds16(xpc + 128u * c + 16u);
+        const uint32_t ra[4] = {wa.x, wa.y, wa.z, wa.w}, rb4[4] = {wb.x, wb.y, wb.z, wb.w};
+        const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t a[4] = {cvt_pair<InT, FMT, 0>(ra[q]), cvt_pair<InT, FMT, 0>(rb4[q]),
+                                 cvt_pair<InT, FMT, 1>(ra[q]), cvt_pair<InT, FMT, 1>(rb4[q])};
+          mma16816<InT>(acc[q % kAcc], a, xw[2 * q], xw[2 * q + 1]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar::arrive(mbar::saddr(&empty[s]));
+    if (pc != P - 1) continue;
+    float v4[4] = {acc[0][0], acc[0][1], acc[0][2], acc[0][3]};
+#pragma unroll
+    for (int a = 1; a < kAcc; ++a)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v4[e] += acc[a][e];
+    // v4[0..1]: block row g, tokens 2t, 2t+1; v4[2..3]: row g + 8
+    float (&rd)[kConsumers][16][8] = red[rb & 1];
+    rd[cw][g][2 * t] = v4[0];
+    rd[cw][g][2 * t + 1] = v4[1];
+    rd[cw][g + 8][2 * t] = v4[2];
+    rd[cw][g + 8][2 * t + 1] = v4[3];
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    if (ctid < 16 * 8) {
+      const int tok = ctid >> 4, row = ctid & 15;
+      if (tok < p.M && out_row < r1) {
+        float v = 0.f;
+#pragma unroll
+        for (int q = 0; q < kConsumers; ++q) v += rd[q][row][tok];
+        reinterpret_cast<OutT*>(p.y)[(size_t)tok * p.N + out_row] = from_f32<OutT>(v * out_scale);
+      }
+    }
+  }
+}
+
+// Shared-memory plan for M tokens and K; stages == 0 means "not applicable".
+// A row block is 16 rows; K is cut into the fewest pieces (each a multiple of
+// 64 bytes, at least kMinRowCopy bytes when cut) that leave room for x and at
+// least three slabs (two when x is large).
+constexpr int kMinRowCopy = 3072;
+Plan plan(int64_t M, int64_t N, int64_t K) {
+  Plan pl = {};
+  if (M < 1 || M > 8 || K % 64 != 0 || K <= 0 || N <= 0 || K > (1 << 20)) return pl;
+  pl.x_bytes = (int)(((M * K * 2) + 127) / 128 * 128);
+  const int64_t room = kSmemBudget - pl.x_bytes;
+  if (room <= 0) return pl;
+  for (int want = 3; want >= 2 && pl.stages == 0; --want) {
+    for (int64_t P = 1; P <= 16; ++P) {
+      if (K % (64 * P) != 0) continue;
+      const int64_t ks = K / P;
+      if (P > 1 && ks < kMinRowCopy) break;
+      const int64_t st = room / (kSlabRows * ks);
+      if (st >= want) {
+        pl.pieces = (int)P;
+        pl.ks = (int)ks;
+        pl.slab_bytes = (int)(kSlabRows * ks);
+        pl.stages = (int)std::min<int64_t>(st, kMaxStages);
+        break;
+      }
+    }
+  }
+  if (pl.stages == 0) return pl;
+  pl.smem = pl.x_bytes + pl.stages * pl.slab_bytes;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  pl.grid = (int)std::min<int64_t>(sms, (N + kSlabRows - 1) / kSlabRows);
+  return pl;
+}
+
+template <typename InT, int FMT, int SCALE, typename OutT>
+int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
+  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT>;
+  static int configured_smem[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_smem[dev & 63] < pl.smem) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget) != cudaSuccess)
+      return CEK_ERR_LAUNCH;
+    configured_smem[dev & 63] = kSmemBudget;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)pl.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)pl.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p, pl) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
+}
+
+template <typename InT, typename OutT>
+int dispatch(const GemvParams& p, const Plan& pl, int w_fmt, int scale_kind, cudaStream_t st) {
+#define CEK_CASE(F, S) \
+  if (w_fmt == F && scale_kind == S) return launch<InT, F, S, OutT>(p, pl, st);
+  CEK_CASE(CEK_E4M3, CEK_SCALE_PERN_F16)
+  CEK_CASE(CEK_E4M3, CEK_SCALE_PERN_F32)
+  CEK_CASE(CEK_E4M3, CEK_SCALE_PERT_F32)
+  CEK_CASE(CEK_E5M2, CEK_SCALE_PERN_F16)
+  CEK_CASE(CEK_E5M2, CEK_SCALE_PERN_F32)
+  CEK_CASE(CEK_E5M2, CEK_SCALE_PERT_F32)
+#undef CEK_CASE
+  return CEK_ERR_INVALID_ARG;
+}
+
+}  // namespace bulk
+
+// The bulk path for a plain GEMV call, or CEK_ERR_UNSUPPORTED when the call
+// does not fit it (more than 8 tokens, K % 64 != 0, or x plus two slabs over
+// the shared-memory budget).  x and w must be 16-byte aligned.
+int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, int scale_kind, cudaStream_t st) {
+  static const bool disabled = [] {
+    const char* v = std::getenv("CEK_GEMV_BULK");
+    return v && v[0] == '0';
+  }();
+  if (disabled) return CEK_ERR_UNSUPPORTED;
+  const bulk::Plan pl = bulk::plan(p.M, p.N, p.K);
+  if (pl.stages == 0) return CEK_ERR_UNSUPPORTED;
+  if (x_dtype == CEK_F16 && y_dtype == CEK_F16) return bulk::dispatch<__half, __half>(p, pl, w_fmt, scale_kind, st);
+  if (x_dtype == CEK_F16 && y_dtype == CEK_BF16)
+    return bulk::dispatch<__half, __nv_bfloat16>(p, pl, w_fmt, scale_kind, st);
+  if (x_dtype == CEK_BF16 && y_dtype == CEK_F16)
+    return bulk::dispatch<__nv_bfloat16, __half>(p, pl, w_fmt, scale_kind, st);
+  return bulk::dispatch<__nv_bfloat16, __nv_bfloat16>(p, pl, w_fmt, scale_kind, st);
+}
+
+}  // namespace cek
+
+extern "C" int cek_gemv_fp8_timeouts(uint64_t* count) {
+  if (!count) return CEK_ERR_INVALID_ARG;
+  unsigned long long v = 0;
+  if (cudaMemcpyFromSymbol(&v, cek::bulk::g_timeouts, sizeof(v)) != cudaSuccess) return CEK_ERR_LAUNCH;
+  *count = v;
+  return CEK_OK;
+}

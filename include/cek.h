@@ -233,6 +233,11 @@ CEK_API int cek_gemm_fp8w(const void* x, const void* w, const void* scale, void*
                           void* workspace, int64_t workspace_bytes, int64_t M, int64_t N,
                           int64_t K, int dtype, int w_fmt, int scale_kind, void* stream);
 
+/* Number of bounded device waits in the bulk-copy GEMV kernel (the
+ * cek_gemv_fp8 path for up to 8 tokens) that gave up since the library was
+ * loaded (0 in a healthy run).  Synchronous. */
+CEK_API int cek_gemv_fp8_timeouts(uint64_t* count);
+
 /* Number of bounded device waits in cek_gemm_fp8_scaled kernels that gave up
  * since the library was loaded (0 in a healthy run).  Synchronous. */
 CEK_API int cek_gemm_fp8_timeouts(uint64_t* count);

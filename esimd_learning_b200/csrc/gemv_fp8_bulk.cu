@@ -5,34 +5,38 @@
 // Same contract as the split-K kernel in gemv_fp8.cu (the reference's
 // GEMV_fp8_pern_kernel / GEMV_fp8_pert_kernel, csrc/xpu/esimd_kernels/
 // fp8_GEMV_v2.h:44-90, 322-368); this is the path for up to 8 tokens when x
-// and a few weight slabs fit in shared memory (8 * K bytes per slab).
+// [M, K] and at least two weight slabs fit in shared memory.
 //
 // Why a second kernel.  With register-held weights every warp spends the
 // FP8 conversion and MMA time of a batch before it reissues that batch's
 // loads, so the bytes in flight per SM drop below what HBM needs, and each
 // warp walks 16 rows 4 KB apart, which costs DRAM row locality.  Measured on
-// gate_up (28672 x 4096): loads alone 18.9 us, with the math 24-26 us.  Here
-// the weight stream is decoupled from the math:
-//  * Persistent grid, one CTA per SM (grid = min(SMs, N / 8)).  CTA c owns
+// gate_up (28672 x 4096, CUDA graph, cold L2): loads alone 18.9 us, the
+// register kernel 31 us, this kernel 21-22 us.  The weight stream is
+// decoupled from the math:
+//  * Persistent grid, one CTA per SM (grid = min(SMs, N / 16)).  CTA c owns
 //    the contiguous rows [N c / G, N (c + 1) / G): every CTA streams the same
 //    byte count to within one row, with no cross-CTA reduction, because a
 //    row's output needs only that row.
-//  * Warp 0, one lane: producer.  Consecutive rows are contiguous in memory,
-//    so a slab of 8 rows x K is one contiguous range; it is fetched with 1-D
-//    cp.async.bulk copies of up to 8 KB into a ring of slabs in shared memory
+//  * Warp 0: producer.  A row block is 16 rows.  Consecutive rows are
+//    contiguous in memory, so with whole rows per slab (K small enough) a
+//    slab is one contiguous range, copied with 1-D cp.async.bulk in 8 KB
+//    parts; for long rows K is cut into P pieces and a slab is 16 row
+//    segments, one copy per lane.  Slabs land in a ring in shared memory
 //    (completion by transaction-count mbarriers; no multicast).  x [M, K] is
 //    copied once per CTA.
-//  * Warps 1-8: consumers.  Slab rows are the n = 8 columns of an
-//    mma.sync m16n8k16 (tokens are the 16 A rows, M <= 8 of them used); each
-//    consumer takes every 8th 64-k chunk of the slab, converts its FP8 bytes
-//    exactly to f16x2 / bf16x2 and accumulates in fp32.  The stage is handed
-//    back right after its last shared-memory read; the 8 partial sums of a
-//    slab are reduced through shared memory in a fixed order (deterministic
-//    results), scaled, converted and stored.
-//  * K permutation: lane (g, t) reads 16 contiguous bytes of slab row g at
-//    k = 64c + 16t and the 16 matching activations; word q feeds MMA step q
-//    (k labels 2t, 2t+1, 2t+8, 2t+9).  Any k bijection shared by both
-//    operands leaves the sum unchanged.
+//  * Warps 1-8: consumers.  The 16 slab rows are the A operand of an
+//    mma.sync m16n8k16, the tokens the 8 B columns (tokens >= M compute
+//    values that are never stored); each consumer takes every 8th 64-k chunk
+//    of a slab, converts its FP8 bytes exactly to f16x2 / bf16x2 and
+//    accumulates in fp32 across the K pieces of the row block.  A stage is
+//    handed back right after its last shared-memory read; the 8 partial sums
+//    of a row block are reduced through shared memory in a fixed order
+//    (deterministic results), scaled, converted and stored.
+//  * K permutation: lane (g, t) reads 16 contiguous bytes of rows g and g+8
+//    at k = 64c + 16t and the 16 matching activations of token g; word q
+//    feeds MMA step q.  Any k bijection shared by both operands leaves the
+//    sum unchanged.
 //  * PDL: griddepcontrol.launch_dependents at CTA start; x is copied after
 //    griddepcontrol.wait; with `early_weights` the first slabs are requested
 //    before the wait.
@@ -47,33 +51,36 @@
 namespace cek {
 namespace bulk {
 
-#ifndef CEK_BULK_CONSUMERS
-#define CEK_BULK_CONSUMERS 8
-#endif
-#ifndef CEK_BULK_NACC
-#define CEK_BULK_NACC 2
-#endif
-constexpr int kConsumers = CEK_BULK_CONSUMERS;
-constexpr int kAcc = CEK_BULK_NACC;  // independent accumulators (shorter MMA dependency chains)
+constexpr int kConsumers = 8;
+constexpr int kAcc = 2;  // independent accumulators (shorter MMA dependency chains)
 constexpr int kThreads = 32 * (1 + kConsumers);
-constexpr int kSlabRows = 16;
+constexpr int kSlabRows = 16;  // a row block: the m16 A operand of the MMA
 constexpr int kMaxStages = 8;
-constexpr uint32_t kPiece = 8192;          // bytes per bulk copy
-constexpr int kSmemBudget = 216 * 1024;    // dynamic shared memory per CTA (static: ~4.2 KB)
+constexpr uint32_t kPiece = 8192;          // bytes per bulk copy of a contiguous slab
+constexpr int kSmemBudget = 216 * 1024;    // dynamic shared memory per CTA (static: ~8.3 KB)
 constexpr uint32_t kWaitPolls = 1u << 22;
+constexpr int kXBatch = 4;                 // chunks per batch when x is read from global memory
 
 __device__ unsigned long long g_timeouts;
+#ifdef CEK_BULK_TRACE
+__device__ unsigned long long g_trace[8192][8];
+__device__ unsigned int g_trace_n;
+CEK_DEVICE unsigned long long gtime() { unsigned long long t; asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t)); return t; }
+#define TRACE(slot, idx) do { if ((slot) < 8192) g_trace[(slot)][(idx)] = gtime(); } while (0)
+#else
+#define TRACE(slot, idx) do { } while (0)
+#endif
 
 // x_bytes: x staged in shared memory; ks: bytes of a row per slab (K / pieces);
 // slab_bytes = 16 * ks.
-struct Plan { int x_bytes, ks, pieces, slab_bytes, stages, smem, grid; };
+struct Plan { int x_bytes, ks, pieces, slab_bytes, stages, smem, grid; };  // x_bytes == 0: x read from global memory
 
-template <typename InT, int FMT, int SCALE, typename OutT>
+template <typename InT, int FMT, int SCALE, typename OutT, bool XG>
 __global__ void __launch_bounds__(kThreads, 1)
 gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], xbar;
-  __shared__ float red[2][kConsumers][16][8];  // [row block parity][consumer][row][token]
+  __shared__ float red[2][kConsumers][kSlabRows][8];  // [row block parity][consumer][row][token]  // [row block parity][consumer][row][token]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = p.K, KS = pl.ks, P = pl.pieces;
@@ -93,6 +100,18 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   }
   __syncthreads();
   pdl_launch_dependents();
+#ifdef CEK_BULK_TRACE
+  __shared__ unsigned trace_slot;
+  if (threadIdx.x == 0) {
+    trace_slot = atomicAdd(&g_trace_n, 1u);
+    if (trace_slot < 8192) { g_trace[trace_slot][0] = (unsigned long long)p.N * 1000000ull + p.M; g_trace[trace_slot][1] = blockIdx.x; }
+    TRACE(trace_slot, 2);
+  }
+  __syncthreads();
+  const unsigned tslot = trace_slot;
+#else
+  const unsigned tslot = 0;
+#endif
 
   if (warp == 0) {
     // Producer warp.  A whole-row slab (P == 1) is one contiguous range,
@@ -124,7 +143,8 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     if (p.early_weights)
       for (int i = 0; i < pre; ++i) issue(i);
     pdl_wait();
-    if (lane == 0) {
+    if (lane == 0) TRACE(tslot, 3);
+    if (!XG && lane == 0) {
       const uint32_t xb = (uint32_t)p.M * (uint32_t)K * 2u;
       const uint32_t bar = mbar::saddr(&xbar);
       mbar::arrive_expect_tx(bar, xb);
@@ -144,6 +164,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       }
       issue(i);
     }
+    if (lane == 0) TRACE(tslot, 4);
     return;
   }
 
@@ -151,10 +172,29 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   const int cw = warp - 1, g = lane >> 2, t = lane & 3;
   const int ctid = threadIdx.x - 32;
   // Tokens >= M read token 0's activations: their output columns are never stored.
-  const uint32_t xrow = mbar::saddr(smem) + (uint32_t)(g < p.M ? g : 0) * K * 2u + 32u * t;
+  const int xtok = g < p.M ? g : 0;
+  const uint32_t xrow = mbar::saddr(smem) + (uint32_t)xtok * K * 2u + 32u * t;
+  const InT* xglob = reinterpret_cast<const InT*>(p.x) + (size_t)xtok * K + 16 * t;
   const int nchunks = KS / 64;
-  bool dead = !mbar::wait(mbar::saddr(&xbar), 0, kWaitPolls);
-  if (dead && lane == 0) atomicAdd(&g_timeouts, 1ull);
+  bool dead = false;
+  // x may be read from global memory (L2) only after the previous kernel
+  // has completed; the shared-memory copy of x arrives behind the weight
+  // slabs requested early, so until it lands the slabs use the global path.
+  pdl_wait();
+  bool x_smem = false;
+  if (cw == 0 && lane == 0) TRACE(tslot, 5);
+
+  // one 64-k chunk: rows g, g+8 (16 bytes each) against 16 activations of token g
+  auto chunk_mma = [&](float (&ac)[kAcc][4], const uint4& wa, const uint4& wb, const uint4& xa, const uint4& xb) {
+    const uint32_t ra[4] = {wa.x, wa.y, wa.z, wa.w}, rb4[4] = {wb.x, wb.y, wb.z, wb.w};
+    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t a[4] = {cvt_pair<InT, FMT, 0>(ra[q]), cvt_pair<InT, FMT, 0>(rb4[q]),
+                             cvt_pair<InT, FMT, 1>(ra[q]), cvt_pair<InT, FMT, 1>(rb4[q])};
+      mma16816<InT>(ac[q % kAcc], a, xw[2 * q], xw[2 * q + 1]);
+    }
+  };
 
   float acc[kAcc][4];
   float out_scale = 0.f;
@@ -166,28 +206,41 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       // now, so the load's latency hides behind the block's math
 #pragma unroll
       for (int a = 0; a < kAcc; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.f;
-      out_row = r0 + rb * kSlabRows + (ctid & 15);
-      out_scale = (ctid < 16 * 8 && out_row < r1) ? load_scale<SCALE>(p.scale, out_row) : 0.f;
+      out_row = r0 + rb * kSlabRows + (ctid % kSlabRows);
+      out_scale = (ctid < kSlabRows * 8 && out_row < r1) ? load_scale<SCALE>(p.scale, out_row) : 0.f;
     }
     if (!dead && !mbar::wait(mbar::saddr(&full[s]), (i / stages) & 1, kWaitPolls)) {
       dead = true;
       if (lane == 0) atomicAdd(&g_timeouts, 1ull);
     }
+    if (i == 0 && cw == 0 && lane == 0) TRACE(tslot, 7);
     const uint32_t wrow = mbar::saddr(smem + pl.x_bytes) + (uint32_t)s * pl.slab_bytes + (uint32_t)g * KS + 16u * t;
     const uint32_t wrow8 = wrow + 8u * KS;
-    const uint32_t xpc = xrow + (uint32_t)pc * KS * 2u;
+    if (!XG && !x_smem) x_smem = __shfl_sync(0xffffffffu, lane == 0 ? mbar::try_wait(mbar::saddr(&xbar), 0) : false, 0);
     if (!dead) {
+      if (x_smem) {
+        const uint32_t xpc = xrow + (uint32_t)pc * KS * 2u;
 #pragma unroll 2
-      for (int c = cw; c < nchunks; c += kConsumers) {
-        const uint4 wa = mbar::lds16(wrow + 64u * c), wb = mbar::lds16(wrow8 + 64u * c);
-        const uint4 xa = mbar::lds16(xpc + 128u * c), xb = mbar::lds16(xpc + 128u * c + 16u);
-        const uint32_t ra[4] = {wa.x, wa.y, wa.z, wa.w}, rb4[4] = {wb.x, wb.y, wb.z, wb.w};
-        const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        for (int c = cw; c < nchunks; c += kConsumers)
+          chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), mbar::lds16(xpc + 128u * c),
+                    mbar::lds16(xpc + 128u * c + 16u));
+      } else {
+        // x from L2: a batch of kXBatch chunks issues all its activation
+        // loads before the first MMA
+        const InT* xpc = xglob + (size_t)pc * KS;
+        for (int c0 = cw; c0 < nchunks; c0 += kXBatch * kConsumers) {
+          uint4 xa[kXBatch], xb[kXBatch];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t a[4] = {cvt_pair<InT, FMT, 0>(ra[q]), cvt_pair<InT, FMT, 0>(rb4[q]),
-                                 cvt_pair<InT, FMT, 1>(ra[q]), cvt_pair<InT, FMT, 1>(rb4[q])};
-          mma16816<InT>(acc[q % kAcc], a, xw[2 * q], xw[2 * q + 1]);
+          for (int u = 0; u < kXBatch; ++u) {
+            const int c = min(c0 + u * kConsumers, nchunks - 1);
+            xa[u] = ldg_nc(xpc + 64 * c);
+            xb[u] = ldg_nc(xpc + 64 * c + 8);
+          }
+#pragma unroll
+          for (int u = 0; u < kXBatch; ++u) {
+            const int c = c0 + u * kConsumers;
+            if (c < nchunks) chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), xa[u], xb[u]);
+          }
         }
       }
     }
@@ -199,15 +252,15 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     for (int a = 1; a < kAcc; ++a)
 #pragma unroll
       for (int e = 0; e < 4; ++e) v4[e] += acc[a][e];
+    float (&rd)[kConsumers][kSlabRows][8] = red[rb & 1];
     // v4[0..1]: block row g, tokens 2t, 2t+1; v4[2..3]: row g + 8
-    float (&rd)[kConsumers][16][8] = red[rb & 1];
     rd[cw][g][2 * t] = v4[0];
     rd[cw][g][2 * t + 1] = v4[1];
     rd[cw][g + 8][2 * t] = v4[2];
     rd[cw][g + 8][2 * t + 1] = v4[3];
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
-    if (ctid < 16 * 8) {
-      const int tok = ctid >> 4, row = ctid & 15;
+    if (ctid < kSlabRows * 8) {
+      const int tok = ctid / kSlabRows, row = ctid % kSlabRows;
       if (tok < p.M && out_row < r1) {
         float v = 0.f;
 #pragma unroll
@@ -216,35 +269,44 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       }
     }
   }
+  // the CTA's shared memory must outlive the x copy into it
+  if (!XG && !x_smem && cw == 0 && !mbar::wait(mbar::saddr(&xbar), 0, kWaitPolls) && lane == 0)
+    atomicAdd(&g_timeouts, 1ull);
+  if (cw == 0 && lane == 0) TRACE(tslot, 6);
 }
 
 // Shared-memory plan for M tokens and K; stages == 0 means "not applicable".
-// A row block is 16 rows; K is cut into the fewest pieces (each a multiple of
-// 64 bytes, at least kMinRowCopy bytes when cut) that leave room for x and at
-// least three slabs (two when x is large).
+// K is cut into the fewest pieces (each a multiple of 64 bytes, and at least
+// kMinRowCopy bytes when cut: smaller copies cost more than they stream)
+// that leave room for x and `want` slabs.  When x [M, K] itself does not fit
+// beside two slabs it is read from global memory (L2) instead.
 constexpr int kMinRowCopy = 3072;
+
+static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want) {
+  const int64_t room = kSmemBudget - x_bytes;
+  if (room <= 0) return false;
+  for (int64_t P = 1; P <= 16; ++P) {
+    if (K % (64 * P) != 0) continue;
+    const int64_t ks = K / P;
+    if (P > 1 && ks < kMinRowCopy) break;
+    const int64_t st = room / (kSlabRows * ks);
+    if (st >= want) {
+      pl.x_bytes = (int)x_bytes;
+      pl.pieces = (int)P;
+      pl.ks = (int)ks;
+      pl.slab_bytes = (int)(kSlabRows * ks);
+      pl.stages = (int)std::min<int64_t>(st, kMaxStages);
+      return true;
+    }
+  }
+  return false;
+}
+
 Plan plan(int64_t M, int64_t N, int64_t K) {
   Plan pl = {};
   if (M < 1 || M > 8 || K % 64 != 0 || K <= 0 || N <= 0 || K > (1 << 20)) return pl;
-  pl.x_bytes = (int)(((M * K * 2) + 127) / 128 * 128);
-  const int64_t room = kSmemBudget - pl.x_bytes;
-  if (room <= 0) return pl;
-  for (int want = 3; want >= 2 && pl.stages == 0; --want) {
-    for (int64_t P = 1; P <= 16; ++P) {
-      if (K % (64 * P) != 0) continue;
-      const int64_t ks = K / P;
-      if (P > 1 && ks < kMinRowCopy) break;
-      const int64_t st = room / (kSlabRows * ks);
-      if (st >= want) {
-        pl.pieces = (int)P;
-        pl.ks = (int)ks;
-        pl.slab_bytes = (int)(kSlabRows * ks);
-        pl.stages = (int)std::min<int64_t>(st, kMaxStages);
-        break;
-      }
-    }
-  }
-  if (pl.stages == 0) return pl;
+  const int64_t xb = ((M * K * 2) + 127) / 128 * 128;
+  if (!try_plan(pl, xb, K, 3) && !try_plan(pl, xb, K, 2) && !try_plan(pl, 0, K, 3)) return Plan{};
   pl.smem = pl.x_bytes + pl.stages * pl.slab_bytes;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -253,9 +315,9 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   return pl;
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT>
+template <typename InT, int FMT, int SCALE, typename OutT, bool XG>
 int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
-  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT>;
+  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XG>;
   static int configured_smem[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -280,7 +342,8 @@ int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
 template <typename InT, typename OutT>
 int dispatch(const GemvParams& p, const Plan& pl, int w_fmt, int scale_kind, cudaStream_t st) {
 #define CEK_CASE(F, S) \
-  if (w_fmt == F && scale_kind == S) return launch<InT, F, S, OutT>(p, pl, st);
+  if (w_fmt == F && scale_kind == S)                                    \
+    return pl.x_bytes ? launch<InT, F, S, OutT, false>(p, pl, st) : launch<InT, F, S, OutT, true>(p, pl, st);
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERN_F16)
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERN_F32)
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERT_F32)
@@ -313,6 +376,16 @@ int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, i
 }
 
 }  // namespace cek
+
+#ifdef CEK_BULK_TRACE
+extern "C" int cek_bulk_trace_read(unsigned long long* host, unsigned* n) {
+  cudaMemcpyFromSymbol(n, cek::bulk::g_trace_n, 4);
+  cudaMemcpyFromSymbol(host, cek::bulk::g_trace, sizeof(unsigned long long) * 8192 * 8);
+  unsigned z = 0;
+  cudaMemcpyToSymbol(cek::bulk::g_trace_n, &z, 4);
+  return 0;
+}
+#endif
 
 extern "C" int cek_gemv_fp8_timeouts(uint64_t* count) {
   if (!count) return CEK_ERR_INVALID_ARG;

@@ -159,6 +159,26 @@ def test_ragged_shapes(cuda_device, M, N, K, io, flags):
     O.assert_parity(y, O.gemv_fp8(x, wq, s), f"M={M} N={N} K={K}")
 
 
+@pytest.mark.parametrize("flags", FLAGS)
+@pytest.mark.parametrize("M,N,K", [(1, 17, 64), (3, 200, 1024), (8, 1001, 512), (7, 33, 2048),
+                                   (2, 2371, 14336), (1, 150, 7168), (5, 4096, 4096), (1, 1, 128),
+                                   (6, 148 * 16 + 5, 3072), (8, 777, 14336), (4, 4096, 14336)])
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_bulk_path_shapes(cuda_device, M, N, K, io, flags):
+    """Shapes the bulk-copy GEMV takes (M <= 8, K % 64 == 0): ragged row
+    ranges per CTA, partial 16-row blocks, K cut into row pieces (K = 7168,
+    14336), grids smaller than the SM count.  No bounded wait may give up."""
+    import ctypes
+    x, wq, s = gemv_case(M, N, K, seed=M * 7919 + N, dtype=io)
+    y = torch.full((M, N), float("nan"), dtype=io, device=cuda_device)
+    cabi_gemv(x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device), y, flags=flags)
+    torch.cuda.synchronize()
+    O.assert_parity(y, O.gemv_fp8(x, wq, s), f"M={M} N={N} K={K}")
+    n = ctypes.c_uint64(99)
+    cabi.call("cek_gemv_fp8_timeouts", ctypes.byref(n))
+    assert n.value == 0
+
+
 def test_mixed_io_dtypes_cabi(cuda_device):
     """The C ABI allows input and output dtypes to differ (the reference host
     code instantiates all four combinations, fp8_GEMV_v2.h:181-190)."""

@@ -305,7 +305,7 @@ def run_ours(args, rank, world, local):
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                 "traffic": traffic, "algorithmic_bytes": STEP_BYTES,
-                "kernel": "cek::gemv_fp8_kernel (12 launches per step; traffic = ncu DRAM bytes per step)"}
+                "kernel": "cek::bulk::gemv_bulk_kernel (12 launches per step; traffic = ncu DRAM bytes per step)"}
 
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,

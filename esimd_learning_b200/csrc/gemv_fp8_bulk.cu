@@ -4,8 +4,8 @@
 //
 // Same contract as the split-K kernel in gemv_fp8.cu (the reference's
 // GEMV_fp8_pern_kernel / GEMV_fp8_pert_kernel, csrc/xpu/esimd_kernels/
-// fp8_GEMV_v2.h:44-90, 322-368); this is the path for up to 8 tokens when x
-// [M, K] and at least two weight slabs fit in shared memory.
+// fp8_GEMV_v2.h:44-90, 322-368); this is the path for up to 8 tokens and
+// K % 64 == 0.
 //
 // Why a second kernel.  With register-held weights every warp spends the
 // FP8 conversion and MMA time of a batch before it reissues that batch's
@@ -24,7 +24,8 @@
 //    parts; for long rows K is cut into P pieces and a slab is 16 row
 //    segments, one copy per lane.  Slabs land in a ring in shared memory
 //    (completion by transaction-count mbarriers; no multicast).  x [M, K] is
-//    copied once per CTA.
+//    copied once per CTA when it fits beside two slabs; otherwise (e.g.
+//    M = 8, K = 14336) the consumers read it from L2 in batches of 8 chunks.
 //  * Warps 1-8: consumers.  The 16 slab rows are the A operand of an
 //    mma.sync m16n8k16, the tokens the 8 B columns (tokens >= M compute
 //    values that are never stored); each consumer takes every 8th 64-k chunk
@@ -39,7 +40,9 @@
 //    sum unchanged.
 //  * PDL: griddepcontrol.launch_dependents at CTA start; x is copied after
 //    griddepcontrol.wait; with `early_weights` the first slabs are requested
-//    before the wait.
+//    before the wait.  The shared copy of x then lands behind those slabs,
+//    so the consumers read x from L2 until it has arrived (measured: the
+//    first MMA ~2.5 us earlier per launch).
 //  * Every mbarrier wait is bounded.  A wait that gives up is counted
 //    (cek_gemv_fp8_timeouts); the CTA stops waiting but keeps its barrier
 //    sequence, so it always exits.
@@ -59,7 +62,8 @@ constexpr int kMaxStages = 8;
 constexpr uint32_t kPiece = 8192;          // bytes per bulk copy of a contiguous slab
 constexpr int kSmemBudget = 216 * 1024;    // dynamic shared memory per CTA (static: ~8.3 KB)
 constexpr uint32_t kWaitPolls = 1u << 22;
-constexpr int kXBatch = 4;                 // chunks per batch when x is read from global memory
+constexpr int kXBatch = 8;                 // chunks per batch when x is read from global memory
+constexpr int kUnroll = 2;                 // chunk loop unroll when x is in shared memory
 
 __device__ unsigned long long g_timeouts;
 #ifdef CEK_BULK_TRACE
@@ -73,7 +77,7 @@ CEK_DEVICE unsigned long long gtime() { unsigned long long t; asm volatile("mov.
 
 // x_bytes: x staged in shared memory; ks: bytes of a row per slab (K / pieces);
 // slab_bytes = 16 * ks.
-struct Plan { int x_bytes, ks, pieces, slab_bytes, stages, smem, grid; };  // x_bytes == 0: x read from global memory
+struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid; };  // x_bytes == 0: x read from global memory
 
 template <typename InT, int FMT, int SCALE, typename OutT, bool XG>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -127,7 +131,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       const uint32_t bar = mbar::saddr(&full[s]);
       if (lane == 0) mbar::arrive_expect_tx(bar, (uint32_t)rows * (uint32_t)KS);
       __syncwarp();
-      if (P == 1) {
+      if (P == 1 && pl.pitch == KS) {
         if (lane == 0) {
           const uint8_t* src = p.w + (size_t)row0 * K;
           const uint32_t bytes = (uint32_t)rows * (uint32_t)K;
@@ -135,7 +139,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
             mbar::bulk_g2s(dst + off, src + off, min(kPiece, bytes - off), bar);
         }
       } else if (lane < rows) {
-        mbar::bulk_g2s(dst + (uint32_t)lane * KS, p.w + (size_t)(row0 + lane) * K + (size_t)pc * KS, (uint32_t)KS,
+        mbar::bulk_g2s(dst + (uint32_t)lane * pl.pitch, p.w + (size_t)(row0 + lane) * K + (size_t)pc * KS, (uint32_t)KS,
                        bar);
       }
     };
@@ -214,13 +218,13 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       if (lane == 0) atomicAdd(&g_timeouts, 1ull);
     }
     if (i == 0 && cw == 0 && lane == 0) TRACE(tslot, 7);
-    const uint32_t wrow = mbar::saddr(smem + pl.x_bytes) + (uint32_t)s * pl.slab_bytes + (uint32_t)g * KS + 16u * t;
-    const uint32_t wrow8 = wrow + 8u * KS;
+    const uint32_t wrow = mbar::saddr(smem + pl.x_bytes) + (uint32_t)s * pl.slab_bytes + (uint32_t)g * pl.pitch + 16u * t;
+    const uint32_t wrow8 = wrow + 8u * pl.pitch;
     if (!XG && !x_smem) x_smem = __shfl_sync(0xffffffffu, lane == 0 ? mbar::try_wait(mbar::saddr(&xbar), 0) : false, 0);
     if (!dead) {
       if (x_smem) {
         const uint32_t xpc = xrow + (uint32_t)pc * KS * 2u;
-#pragma unroll 2
+#pragma unroll (kUnroll)
         for (int c = cw; c < nchunks; c += kConsumers)
           chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), mbar::lds16(xpc + 128u * c),
                     mbar::lds16(xpc + 128u * c + 16u));
@@ -281,6 +285,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
 // that leave room for x and `want` slabs.  When x [M, K] itself does not fit
 // beside two slabs it is read from global memory (L2) instead.
 constexpr int kMinRowCopy = 3072;
+constexpr int kRowPad = 0;  // shared-memory row padding (16 measured no faster)
 
 static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want) {
   const int64_t room = kSmemBudget - x_bytes;
@@ -289,12 +294,14 @@ static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want) {
     if (K % (64 * P) != 0) continue;
     const int64_t ks = K / P;
     if (P > 1 && ks < kMinRowCopy) break;
-    const int64_t st = room / (kSlabRows * ks);
+    const int64_t pitch = ks + kRowPad;
+    const int64_t st = room / (kSlabRows * pitch);
     if (st >= want) {
       pl.x_bytes = (int)x_bytes;
       pl.pieces = (int)P;
       pl.ks = (int)ks;
-      pl.slab_bytes = (int)(kSlabRows * ks);
+      pl.pitch = (int)pitch;
+      pl.slab_bytes = (int)(kSlabRows * pitch);
       pl.stages = (int)std::min<int64_t>(st, kMaxStages);
       return true;
     }

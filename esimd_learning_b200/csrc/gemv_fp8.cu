@@ -306,7 +306,7 @@ static int dispatch_fmt_scale(const GemvParams& p, const GemvLaunch& L, int w_fm
 
 int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
                 bool fused, cudaStream_t st) {
-  if (!fused && base.nmat == 0 && base.ar_world == 0) {
+  if (!fused && base.nmat == 0) {
     const int s = gemv_bulk_launch(base, x_dtype, y_dtype, w_fmt, scale_kind, st);
     if (s != CEK_ERR_UNSUPPORTED) return s;
   }

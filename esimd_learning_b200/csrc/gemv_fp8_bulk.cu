@@ -269,7 +269,17 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
         float v = 0.f;
 #pragma unroll
         for (int q = 0; q < kConsumers; ++q) v += rd[q][row][tok];
-        reinterpret_cast<OutT*>(p.y)[(size_t)tok * p.N + out_row] = from_f32<OutT>(v * out_scale);
+        const OutT o = from_f32<OutT>(v * out_scale);
+        if (p.ar_world == 0) {
+          reinterpret_cast<OutT*>(p.y)[(size_t)tok * p.N + out_row] = o;
+        } else {
+          // tensor-parallel push (tp_allreduce.cu): slot ar_rank of every
+          // rank's receive buffer, slot set chosen by this call's epoch parity
+          const unsigned set = (*reinterpret_cast<volatile unsigned*>(&p.ar_sync[tp::kEpoch]) + 1) & 1u;
+          const size_t off = (((size_t)set * p.ar_world + p.ar_rank) * p.M + tok) * p.N + out_row;
+          for (int r = 0; r < p.ar_world; ++r)
+            reinterpret_cast<OutT*>(p.ar_peers[r] + tp::kSyncBytes)[off] = o;
+        }
       }
     }
   }

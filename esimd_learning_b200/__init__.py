@@ -31,6 +31,8 @@ from esimd_learning_b200.ops import (  # noqa: E402,F401
     esimd_gemm_fp8_pert,
     esimd_fused_add_rms_norm_batched_fp8,
     esimd_gelu_and_mul,
+    esimd_gemv_fp8_gelu_mul,
+    esimd_fused_add_rms_norm_gelu_mul_fp8,
     esimd_qkv_norm_rope,
     esimd_quant_fp8_per_token,
     esimd_set_weight_prefetch,

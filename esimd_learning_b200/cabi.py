@@ -21,6 +21,7 @@ CEK_F16, CEK_BF16 = 0, 1
 CEK_E4M3, CEK_E5M2 = 0, 1
 CEK_SCALE_PERN_F16, CEK_SCALE_PERN_F32, CEK_SCALE_PERT_F32 = 0, 1, 2
 CEK_GEMV_EARLY_WEIGHTS = 1
+CEK_GEMV_GELU_MUL_OUTPUT = 2
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64

@@ -10,15 +10,17 @@ One step, on every rank (rank r of TP):
 2. ``esimd_qkv_norm_rope`` on the local heads (per-head RMSNorm of q and k,
    RoPE theta 500000 at the token positions).  Attention itself is outside
    this path.
-3. ``esimd_fused_add_rms_norm_batched_fp8`` again for the MLP block: residual
+3. ``esimd_fused_add_rms_norm_gelu_mul_fp8`` for the MLP block: residual
    += attention output (given as an input), RMSNorm, the gate_up GEMV over
-   this rank's [gate | up] rows (column-parallel, 57344 / TP rows).
-4. ``esimd_gelu_and_mul`` on the local half-width (28672 / TP).
+   this rank's [gate | up] rows (column-parallel, 57344 / TP rows) with
+4. GeLU(tanh)-and-mul in its epilogue: the local activation [M, 28672 / TP]
+   in one launch of the gated bulk GEMV (M > 8: the GEMV, then
+   ``esimd_gelu_and_mul``).
 5. The down GEMV on this rank's K-slice of the down weight (row-parallel,
    K = 28672 / TP) with the full per-channel scale: a partial sum of the
    output.
-6. NCCL all-reduce (sum) of the fp16 [M, 8192] partials; at TP = 1 it is
-   skipped.
+6. The all-reduce (sum) of the fp16 [M, 8192] partials: fused into the down
+   GEMV over peer memory (``TPComm``) or NCCL; at TP = 1 it is skipped.
 
 All weights are e4m3 with per-output-channel fp32 scales computed on the
 full (unsharded) matrix, so the sharded step equals the unsharded one up to
@@ -194,7 +196,6 @@ class DecodeChain:
         self.cos_sin = rope_cache(shape, device)
         f16 = dict(dtype=torch.float16, device=device)
         self.qkv = torch.empty(M, (lq + 2 * lkv) * d, **f16)
-        self.gu = torch.empty(M, 2 * lf, **f16)
         self.act = torch.empty(M, lf, **f16)
         self.out = torch.empty(M, h, **f16)
         self.graph = None
@@ -206,9 +207,7 @@ class DecodeChain:
         o.esimd_fused_add_rms_norm_batched_fp8(hidden, residual, w["gamma_attn"], s.eps, *w["qkv"], self.qkv)
         o.esimd_qkv_norm_rope(self.qkv, positions, w["q_norm"], w["k_norm"], self.cos_sin, self.lq, self.lkv,
                               s.head_dim, s.eps, True)
-        o.esimd_fused_add_rms_norm_batched_fp8(attn_out, residual, w["gamma_mlp"], s.eps, *w["gate_up"],
-                                               self.gu)
-        o.esimd_gelu_and_mul(self.gu, self.act)
+        o.esimd_fused_add_rms_norm_gelu_mul_fp8(attn_out, residual, w["gamma_mlp"], s.eps, *w["gate_up"], self.act)
         wd, sd = w["down"]
         if self.world > 1 and self.comm is not None:
             c, cb = self.comm, self.comm.cabi

@@ -107,6 +107,29 @@ template <> CEK_DEVICE uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// ---- GeLU(tanh)-and-mul ------------------------------------------------------
+// gelu_tanh(g) = 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))), in fp32 with
+// every rounding step pinned (no contraction choices left to the compiler),
+// so the standalone op and the GEMV prologue that forms the same product
+// produce identical bits.
+CEK_DEVICE float gelu_tanh(float g) {
+  const float kAlpha = 0.7978845608028654f;  // sqrt(2/pi)
+  const float kBeta = 0.044715f;
+  const float inner = __fmul_rn(kAlpha, __fmaf_rn(__fmul_rn(kBeta, __fmul_rn(g, g)), g, g));
+  return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.f, tanhf(inner)));
+}
+// io(gelu_tanh(g) * u) for a packed pair of 16-bit values.
+template <typename T>
+CEK_DEVICE uint32_t gelu_mul2(uint32_t g2, uint32_t u2) {
+  const float2 g = unpack2<T>(g2), u = unpack2<T>(u2);
+  return pack2<T>(__fmul_rn(gelu_tanh(g.x), u.x), __fmul_rn(gelu_tanh(g.y), u.y));
+}
+
+template <typename T>
+CEK_DEVICE T gelu_mul1(T g, T u) {
+  return from_f32<T>(__fmul_rn(gelu_tanh(to_f32<T>(g)), to_f32<T>(u)));
+}
+
 // ---- warp / block reductions -------------------------------------------------
 CEK_DEVICE float warp_sum(float v) {
 #pragma unroll

@@ -18,23 +18,21 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 gelu_and_mul_kernel(const T* __restrict__ x, T* __restrict__ out, int d) {
   const int m = blockIdx.y;
-  const int v = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element vector index
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element group index
   if (v * 8 >= d) return;
   const T* row = x + (size_t)m * 2 * d;
-  const uint4 gv = *reinterpret_cast<const uint4*>(row + v * 8);
-  const uint4 uv = *reinterpret_cast<const uint4*>(row + d + v * 8);
-  const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
-  uint32_t ow[4];
-  const float kAlpha = 0.7978845608028654f;  // sqrt(2/pi)
-  const float kBeta = 0.044715f;
+  if (d % 8 == 0) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(row + v * 8);
+    const uint4 uv = *reinterpret_cast<const uint4*>(row + d + v * 8);
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t ow[4];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float2 g = unpack2<T>(gw[q]), u = unpack2<T>(uw[q]);
-    const float a = 0.5f * g.x * (1.f + tanhf(kAlpha * (g.x + kBeta * g.x * g.x * g.x)));
-    const float b = 0.5f * g.y * (1.f + tanhf(kAlpha * (g.y + kBeta * g.y * g.y * g.y)));
-    ow[q] = pack2<T>(a * u.x, b * u.y);
+    for (int q = 0; q < 4; ++q) ow[q] = gelu_mul2<T>(gw[q], uw[q]);
+    *reinterpret_cast<uint4*>(out + (size_t)m * d + v * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  } else {
+    // rows not 16-byte aligned: element by element, same arithmetic
+    for (int j = v * 8; j < min(d, v * 8 + 8); ++j) out[(size_t)m * d + j] = gelu_mul1<T>(row[j], row[d + j]);
   }
-  *reinterpret_cast<uint4*>(out + (size_t)m * d + v * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
 }
 
 // ---- q/k per-head RMSNorm + rotary embedding -----------------------------------
@@ -160,13 +158,13 @@ quant_fp8_per_token_kernel(const T* __restrict__ a, uint8_t* __restrict__ q, flo
 
 extern "C" int cek_gelu_and_mul(const void* x, void* out, int64_t M, int64_t d, int dtype,
                                 void* stream) {
-  if (M < 0 || d < 0 || d % 8 != 0 || M > 65535) return CEK_ERR_INVALID_ARG;
+  if (M < 0 || d < 0 || M > 65535) return CEK_ERR_INVALID_ARG;
   if (dtype != CEK_F16 && dtype != CEK_BF16) return CEK_ERR_INVALID_ARG;
   if (M == 0 || d == 0) return CEK_OK;
   if (!x || !out) return CEK_ERR_INVALID_ARG;
-  if (!cek_host::aligned16(x) || !cek_host::aligned16(out)) return CEK_ERR_ALIGNMENT;
+  if (d % 8 == 0 && (!cek_host::aligned16(x) || !cek_host::aligned16(out))) return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  dim3 grid((unsigned)((d / 8 + 255) / 256), (unsigned)M), block(256);
+  dim3 grid((unsigned)(((d + 7) / 8 + 255) / 256), (unsigned)M), block(256);
   if (dtype == CEK_F16)
     cek::gelu_and_mul_kernel<__half><<<grid, block, 0, st>>>(
         static_cast<const __half*>(x), static_cast<__half*>(out), (int)d);

@@ -26,6 +26,10 @@ struct GemvParams {
   // guarantees the preceding kernel on the stream does not write them);
   // 0: every global read waits for the preceding kernel.
   int early_weights;
+  // 1: gated GeLU output.  w holds 2N rows, gate rows [0, N) then up rows
+  // [N, 2N) (scale likewise); y [M, N] = io(gelu_tanh(io(gate)) * io(up))
+  // (bulk kernel only)
+  int y_gelu;
   // tensor-parallel all-reduce epilogue (ar_world > 0, tp_allreduce.cu):
   // y is pushed into slot ar_rank of every rank's receive buffer instead of
   // being stored to p.y.

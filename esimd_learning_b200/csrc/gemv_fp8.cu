@@ -306,9 +306,9 @@ static int dispatch_fmt_scale(const GemvParams& p, const GemvLaunch& L, int w_fm
 
 int gemv_launch(const GemvParams& base, int x_dtype, int y_dtype, int w_fmt, int scale_kind,
                 bool fused, cudaStream_t st) {
-  if (!fused && base.nmat == 0) {
+  if (!fused) {
     const int s = gemv_bulk_launch(base, x_dtype, y_dtype, w_fmt, scale_kind, st);
-    if (s != CEK_ERR_UNSUPPORTED) return s;
+    if (s != CEK_ERR_UNSUPPORTED || base.y_gelu) return s;  // only the bulk kernel forms gelu(gate) * up
   }
   GemvLaunch L = plan_gemv(base.M, base.N, base.K);  // multi-GEMV: N = sum of the matrices' N
   GemvParams p = base;
@@ -347,7 +347,7 @@ extern "C" int cek_gemv_fp8(const void* x, const void* w, const void* scale, voi
     return CEK_ERR_INVALID_ARG;
   if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
   if (scale_kind < CEK_SCALE_PERN_F16 || scale_kind > CEK_SCALE_PERT_F32) return CEK_ERR_INVALID_ARG;
-  if (flags & ~(unsigned)CEK_GEMV_EARLY_WEIGHTS) return CEK_ERR_INVALID_ARG;
+  if (flags & ~(unsigned)(CEK_GEMV_EARLY_WEIGHTS | CEK_GEMV_GELU_MUL_OUTPUT)) return CEK_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return CEK_OK;
   if (K % 16 != 0 || N > INT32_MAX || K > INT32_MAX || M > INT32_MAX) return CEK_ERR_INVALID_ARG;
   if (!x || !w || !scale || !y) return CEK_ERR_INVALID_ARG;
@@ -356,6 +356,7 @@ extern "C" int cek_gemv_fp8(const void* x, const void* w, const void* scale, voi
   p.x = x; p.w = static_cast<const uint8_t*>(w); p.scale = scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.early_weights = (flags & CEK_GEMV_EARLY_WEIGHTS) ? 1 : 0;
+  p.y_gelu = (flags & CEK_GEMV_GELU_MUL_OUTPUT) ? 1 : 0;
   return cek::gemv_launch(p, x_dtype, y_dtype, w_fmt, scale_kind, false,
                           static_cast<cudaStream_t>(stream));
 }

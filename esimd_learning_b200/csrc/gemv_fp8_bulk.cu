@@ -79,6 +79,45 @@ CEK_DEVICE unsigned long long gtime() { unsigned long long t; asm volatile("mov.
 // slab_bytes = 16 * ks.
 struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid; };  // x_bytes == 0: x read from global memory
 
+// Row blocks over the rows of one matrix, or of up to kMaxMats matrices
+// sharing x (multi-GEMV, rows concatenated): a block is at most `bsz` rows
+// (16; 8 gate/up row pairs for the gated GeLU output) and never straddles two
+// matrices.
+CEK_DEVICE int mat_rows(const GemvParams& p, int m) { return p.nmat ? p.mns[m] : p.N; }
+CEK_DEVICE int total_rows(const GemvParams& p) {
+  int t = 0;
+  for (int m = 0; m < (p.nmat ? p.nmat : 1); ++m) t += mat_rows(p, m);
+  return t;
+}
+struct BlockCursor {
+  int m, mstart;  // current matrix and its first row in the concatenated numbering
+  int row;        // next concatenated row
+  int end;        // the CTA's end row
+  int bsz;        // rows per block
+  CEK_DEVICE void init(const GemvParams& p, int r0, int r1, int block_rows) {
+    m = 0; mstart = 0; row = r0; end = r1; bsz = block_rows;
+    while (m + 1 < (p.nmat ? p.nmat : 1) && row >= mstart + mat_rows(p, m)) mstart += mat_rows(p, m++);
+  }
+  // the next block: matrix, first row inside the matrix, row count
+  CEK_DEVICE void next(const GemvParams& p, int& bm, int& brow, int& brows) {
+    const int mend = mstart + mat_rows(p, m);
+    const int stop = min(min(row + bsz, end), mend);
+    bm = m; brow = row - mstart; brows = stop - row;
+    row = stop;
+    if (row == mend && m + 1 < (p.nmat ? p.nmat : 1)) { mstart = mend; ++m; }
+  }
+};
+CEK_DEVICE int count_blocks(const GemvParams& p, int r0, int r1, int bsz) {
+  int n = 0, ms = 0;
+  for (int m = 0; m < (p.nmat ? p.nmat : 1); ++m) {
+    const int me = ms + mat_rows(p, m);
+    const int lo = max(r0, ms), hi = min(r1, me);
+    if (hi > lo) n += (hi - lo + bsz - 1) / bsz;
+    ms = me;
+  }
+  return n;
+}
+
 template <typename InT, int FMT, int SCALE, typename OutT, bool XG>
 __global__ void __launch_bounds__(kThreads, 1)
 gemv_bulk_kernel(const GemvParams p, const Plan pl) {
@@ -88,9 +127,13 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = p.K, KS = pl.ks, P = pl.pieces;
-  const int r0 = (int)((int64_t)p.N * blockIdx.x / gridDim.x);
-  const int r1 = (int)((int64_t)p.N * (blockIdx.x + 1) / gridDim.x);
-  const int nblocks = (r1 - r0 + kSlabRows - 1) / kSlabRows;
+  const int nrows = total_rows(p);
+  const int r0 = (int)((int64_t)nrows * blockIdx.x / gridDim.x);
+  const int r1 = (int)((int64_t)nrows * (blockIdx.x + 1) / gridDim.x);
+  // gated GeLU output: a block is 8 gate rows (slab rows 0-7) and the
+  // matching 8 up rows N + j (slab rows 8-15); rows count row pairs
+  const int bsz = p.y_gelu ? kSlabRows / 2 : kSlabRows;
+  const int nblocks = count_blocks(p, r0, r1, bsz);
   const int nslabs = nblocks * P;  // slab i = row block i / P, K piece i % P
   const int stages = pl.stages;
 
@@ -123,24 +166,34 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     // segments, one copy per lane.
     const uint32_t ring = mbar::saddr(smem + pl.x_bytes);
     bool ok = true;
+    BlockCursor cur;
+    cur.init(p, r0, r1, bsz);
+    int bm = 0, brow = 0, rows = 0;
     auto issue = [&](int i) {
-      const int s = i % stages, rb = i / P, pc = i - rb * P;
-      const int row0 = r0 + rb * kSlabRows;
-      const int rows = min(kSlabRows, r1 - row0);
+      const int s = i % stages, pc = i % P;
+      if (pc == 0) cur.next(p, bm, brow, rows);
+      const uint8_t* wm = (p.nmat ? p.mws[bm] : p.w) + (size_t)brow * K;
       const uint32_t dst = ring + (uint32_t)s * pl.slab_bytes;
       const uint32_t bar = mbar::saddr(&full[s]);
-      if (lane == 0) mbar::arrive_expect_tx(bar, (uint32_t)rows * (uint32_t)KS);
+      if (lane == 0) mbar::arrive_expect_tx(bar, (p.y_gelu ? 2u : 1u) * (uint32_t)rows * (uint32_t)KS);
       __syncwarp();
       if (P == 1 && pl.pitch == KS) {
         if (lane == 0) {
-          const uint8_t* src = p.w + (size_t)row0 * K;
           const uint32_t bytes = (uint32_t)rows * (uint32_t)K;
           for (uint32_t off = 0; off < bytes; off += kPiece)
-            mbar::bulk_g2s(dst + off, src + off, min(kPiece, bytes - off), bar);
+            mbar::bulk_g2s(dst + off, wm + off, min(kPiece, bytes - off), bar);
+          if (p.y_gelu) {
+            const uint8_t* wu = wm + (size_t)p.N * K;
+            for (uint32_t off = 0; off < bytes; off += kPiece)
+              mbar::bulk_g2s(dst + 8u * pl.pitch + off, wu + off, min(kPiece, bytes - off), bar);
+          }
         }
-      } else if (lane < rows) {
-        mbar::bulk_g2s(dst + (uint32_t)lane * pl.pitch, p.w + (size_t)(row0 + lane) * K + (size_t)pc * KS, (uint32_t)KS,
-                       bar);
+      } else if (!p.y_gelu) {
+        if (lane < rows)
+          mbar::bulk_g2s(dst + (uint32_t)lane * pl.pitch, wm + (size_t)lane * K + (size_t)pc * KS, (uint32_t)KS, bar);
+      } else if (lane < 16 && (lane & 7) < rows) {
+        const uint8_t* src = wm + (lane >= 8 ? (size_t)p.N * K : 0) + (size_t)(lane & 7) * K + (size_t)pc * KS;
+        mbar::bulk_g2s(dst + (uint32_t)lane * pl.pitch, src, (uint32_t)KS, bar);
       }
     };
     const int pre = min(stages, nslabs);
@@ -201,17 +254,24 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   };
 
   float acc[kAcc][4];
-  float out_scale = 0.f;
-  int out_row = 0;
+  float out_scale = 0.f, out_scale_up = 0.f;
+  int out_row = 0;  // row inside the block's matrix of this thread's output
+  bool out_ok = false;
+  int bm = 0, brow = 0, brows = 0;
+  BlockCursor cur;
+  cur.init(p, r0, r1, bsz);
   for (int i = 0; i < nslabs; ++i) {
     const int s = i % stages, rb = i / P, pc = i - rb * P;
     if (pc == 0) {
       // new row block: clear the sums; the epilogue thread fetches its scale
       // now, so the load's latency hides behind the block's math
+      cur.next(p, bm, brow, brows);
 #pragma unroll
       for (int a = 0; a < kAcc; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.f;
-      out_row = r0 + rb * kSlabRows + (ctid % kSlabRows);
-      out_scale = (ctid < kSlabRows * 8 && out_row < r1) ? load_scale<SCALE>(p.scale, out_row) : 0.f;
+      out_row = brow + (ctid % bsz);
+      out_ok = ctid < bsz * 8 && (ctid % bsz) < brows;
+      out_scale = out_ok ? load_scale<SCALE>(p.nmat ? p.mscales[bm] : p.scale, out_row) : 0.f;
+      if (p.y_gelu) out_scale_up = out_ok ? load_scale<SCALE>(p.scale, p.N + out_row) : 0.f;
     }
     if (!dead && !mbar::wait(mbar::saddr(&full[s]), (i / stages) & 1, kWaitPolls)) {
       dead = true;
@@ -263,15 +323,25 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     rd[cw][g + 8][2 * t] = v4[2];
     rd[cw][g + 8][2 * t + 1] = v4[3];
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
-    if (ctid < kSlabRows * 8) {
-      const int tok = ctid / kSlabRows, row = ctid % kSlabRows;
-      if (tok < p.M && out_row < r1) {
+    if (ctid < bsz * 8) {
+      const int tok = ctid / bsz, row = ctid % bsz;
+      if (tok < p.M && out_ok) {
         float v = 0.f;
 #pragma unroll
         for (int q = 0; q < kConsumers; ++q) v += rd[q][row][tok];
-        const OutT o = from_f32<OutT>(v * out_scale);
+        OutT o = from_f32<OutT>(v * out_scale);
+        if (p.y_gelu) {
+          // the up row of the pair sits 8 slab rows below the gate row; each
+          // is rounded to the output type first, as the unfused GEMV stores
+          // them, then io(gelu_tanh(gate) * up)
+          float u = 0.f;
+#pragma unroll
+          for (int q = 0; q < kConsumers; ++q) u += rd[q][row + 8][tok];
+          o = gelu_mul1<OutT>(o, from_f32<OutT>(u * out_scale_up));
+        }
         if (p.ar_world == 0) {
-          reinterpret_cast<OutT*>(p.y)[(size_t)tok * p.N + out_row] = o;
+          const int nm = p.nmat ? p.mns[bm] : p.N;
+          reinterpret_cast<OutT*>(p.nmat ? p.mys[bm] : p.y)[(size_t)tok * nm + out_row] = o;
         } else {
           // tensor-parallel push (tp_allreduce.cu): slot ar_rank of every
           // rank's receive buffer, slot set chosen by this call's epoch parity
@@ -374,16 +444,17 @@ int dispatch(const GemvParams& p, const Plan& pl, int w_fmt, int scale_kind, cud
 }  // namespace bulk
 
 // The bulk path for a plain GEMV call, or CEK_ERR_UNSUPPORTED when the call
-// does not fit it (more than 8 tokens, K % 64 != 0, or x plus two slabs over
-// the shared-memory budget).  x and w must be 16-byte aligned.
+// does not fit it (more than 8 tokens or K % 64 != 0; the gated GeLU output
+// also needs a single matrix without the all-reduce push).  x and w must be
+// 16-byte aligned.
 int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, int scale_kind, cudaStream_t st) {
   static const bool disabled = [] {
     const char* v = std::getenv("CEK_GEMV_BULK");
     return v && v[0] == '0';
   }();
   if (disabled) return CEK_ERR_UNSUPPORTED;
-  const bulk::Plan pl = bulk::plan(p.M, p.N, p.K);
-  if (pl.stages == 0) return CEK_ERR_UNSUPPORTED;
+  const bulk::Plan pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K);
+  if (pl.stages == 0 || (p.y_gelu && (p.nmat || p.ar_world))) return CEK_ERR_UNSUPPORTED;
   if (x_dtype == CEK_F16 && y_dtype == CEK_F16) return bulk::dispatch<__half, __half>(p, pl, w_fmt, scale_kind, st);
   if (x_dtype == CEK_F16 && y_dtype == CEK_BF16)
     return bulk::dispatch<__half, __nv_bfloat16>(p, pl, w_fmt, scale_kind, st);

@@ -174,9 +174,12 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
   if (M > 16 || N < 0 || workspace_bytes < 0) return CEK_ERR_INVALID_ARG;
   if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
   if (scale_kind < CEK_SCALE_PERN_F16 || scale_kind > CEK_SCALE_PERT_F32) return CEK_ERR_INVALID_ARG;
-  if (flags & ~(unsigned)CEK_GEMV_EARLY_WEIGHTS) return CEK_ERR_INVALID_ARG;
+  if (flags & ~(unsigned)(CEK_GEMV_EARLY_WEIGHTS | CEK_GEMV_GELU_MUL_OUTPUT)) return CEK_ERR_INVALID_ARG;
   if (M == 0) return CEK_OK;
   if (!norm_weight || !w || !scale || !workspace || (N > 0 && !y)) return CEK_ERR_INVALID_ARG;
+  const bool gelu_out = (flags & CEK_GEMV_GELU_MUL_OUTPUT) != 0;
+  // the gated output is formed by the bulk GEMV, which reads staged rows
+  if (gelu_out && (workspace_bytes < normed_bytes(M, K) || M > 8 || K % 64 != 0)) return CEK_ERR_UNSUPPORTED;
   if (workspace_bytes < inv_rms_bytes(M)) return CEK_ERR_INVALID_ARG;
   if (!cek_host::aligned16(norm_weight) || !cek_host::aligned16(w) || !cek_host::aligned16(workspace))
     return CEK_ERR_ALIGNMENT;
@@ -200,7 +203,7 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   // The stats kernel never writes W: the GEMV may always prefetch it.
   p.early_weights = 1;
-  (void)flags;
+  p.y_gelu = gelu_out ? 1 : 0;
   if (staged) {
     p.x = workspace;
     return cek::gemv_launch(p, dtype, dtype, w_fmt, scale_kind, false, st);

@@ -189,6 +189,88 @@ at::Tensor esimd_gelu_and_mul(at::Tensor input, at::Tensor output) {
   return output;
 }
 
+// New: output [M, N] = gelu_tanh(g) * u with [g | u] = GEMV(input, weight
+// [2N, K]) rounded to the io dtype: the decode MLP's gate_up projection with
+// GeLU-and-mul fused into its epilogue (cek_gemv_fp8 with
+// CEK_GEMV_GELU_MUL_OUTPUT).  Shapes the fused kernel does not take run as
+// the GEMV into a [M, 2N] temporary followed by esimd_gelu_and_mul, which is
+// the same arithmetic.
+at::Tensor esimd_gemv_fp8_gelu_mul(at::Tensor input, at::Tensor weight, at::Tensor weight_scale,
+                                   at::Tensor output) {
+  const char* op = "esimd_gemv_fp8_gelu_mul";
+  check_cuda(input, op, "input");
+  check_cuda(weight, op, "weight");
+  check_cuda(weight_scale, op, "weight_scale");
+  check_cuda(output, op, "output");
+  check_gemv_io(input, output, op);
+  TORCH_CHECK(weight.dim() == 2 && weight.size(0) % 2 == 0, op, ": weight must be [2N, K]");
+  const int64_t N = weight.size(0) / 2, K = weight.size(1);
+  TORCH_CHECK(K > 0 && input.size(-1) == K, op, ": input must be [M, K]");
+  const int64_t M = input.numel() / K;
+  TORCH_CHECK(output.numel() == M * N, op, ": output must be [M, N]");
+  const int fmt = fp8_format(weight, op);
+  const int sk = scale_kind(weight_scale, 2 * N, true, op);
+  c10::cuda::CUDAGuard guard(input.device());
+  const int rc = cek_gemv_fp8(input.data_ptr(), weight.data_ptr(), weight_scale.data_ptr(), output.data_ptr(), M, N,
+                              K, io_dtype(input), io_dtype(output), fmt, sk, gemv_flags() | CEK_GEMV_GELU_MUL_OUTPUT,
+                              stream_of(input));
+  if (rc != CEK_ERR_UNSUPPORTED) {
+    check_status(rc, op);
+    return output;
+  }
+  at::Tensor gu = at::empty({M, 2 * N}, output.options());
+  check_status(cek_gemv_fp8(input.data_ptr(), weight.data_ptr(), weight_scale.data_ptr(), gu.data_ptr(), M, 2 * N,
+                            K, io_dtype(input), io_dtype(gu), fmt, sk, gemv_flags(), stream_of(input)),
+               op);
+  check_status(cek_gelu_and_mul(gu.data_ptr(), output.data_ptr(), M, N, io_dtype(gu), stream_of(input)), op);
+  return output;
+}
+
+// New: esimd_fused_add_rms_norm_batched_fp8 whose projection is the gated
+// gate_up one above: residual += hidden; hidden = RMSNorm(residual) * weight;
+// output [M, N] = gelu_tanh(g) * u, [g | u] = GEMV(hidden, qweight [2N, K]).
+at::Tensor esimd_fused_add_rms_norm_gelu_mul_fp8(at::Tensor hidden_states, at::Tensor residual, at::Tensor weight,
+                                                 double eps, at::Tensor qweight, at::Tensor qweight_scale,
+                                                 at::Tensor output) {
+  const char* op = "esimd_fused_add_rms_norm_gelu_mul_fp8";
+  check_cuda(hidden_states, op, "hidden_states");
+  check_cuda(residual, op, "residual");
+  check_cuda(weight, op, "weight");
+  check_cuda(qweight, op, "qweight");
+  check_cuda(qweight_scale, op, "qweight_scale");
+  check_cuda(output, op, "output");
+  TORCH_CHECK(is_half_or_bf16(hidden_states), op, ": hidden_states must be fp16 or bf16");
+  TORCH_CHECK(residual.scalar_type() == hidden_states.scalar_type() &&
+                  weight.scalar_type() == hidden_states.scalar_type() &&
+                  output.scalar_type() == hidden_states.scalar_type(),
+              op, ": hidden_states, residual, weight and output must share a dtype");
+  TORCH_CHECK(qweight.dim() == 2 && qweight.size(0) % 2 == 0, op, ": qweight must be [2N, K]");
+  const int64_t N = qweight.size(0) / 2, K = qweight.size(1);
+  TORCH_CHECK(hidden_states.size(-1) == K && residual.numel() == hidden_states.numel(), op,
+              ": hidden_states/residual must be [M, K]");
+  TORCH_CHECK(weight.numel() == K, op, ": weight must have K elements");
+  const int64_t M = hidden_states.numel() / K;
+  TORCH_CHECK(M <= 16, op, ": at most 16 rows");
+  TORCH_CHECK(output.numel() == M * N, op, ": output must hold M*N elements");
+  const int fmt = fp8_format(qweight, op);
+  const int sk = scale_kind(qweight_scale, 2 * N, true, op);
+  c10::cuda::CUDAGuard guard(hidden_states.device());
+  const int64_t ws_bytes = cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, K);
+  at::Tensor ws = at::empty({ws_bytes}, hidden_states.options().dtype(at::kByte));
+  const bool fused = M <= 8 && K % 64 == 0;  // what the gated bulk GEMV takes
+  at::Tensor gu = fused ? output : at::empty({M, 2 * N}, output.options());
+  check_status(cek_fused_add_rmsnorm_gemv_fp8(hidden_states.data_ptr(), residual.data_ptr(), weight.data_ptr(),
+                                              (float)eps, qweight.data_ptr(), qweight_scale.data_ptr(), gu.data_ptr(),
+                                              ws.data_ptr(), ws_bytes, M, fused ? N : 2 * N, K,
+                                              io_dtype(hidden_states), fmt, sk,
+                                              fused ? CEK_GEMV_GELU_MUL_OUTPUT : 0u, stream_of(hidden_states)),
+               op);
+  if (!fused)
+    check_status(cek_gelu_and_mul(gu.data_ptr(), output.data_ptr(), M, N, io_dtype(gu), stream_of(hidden_states)),
+                 op);
+  return output;
+}
+
 // New: per-head RMSNorm on q and k heads, then rotary embedding, in place.
 at::Tensor esimd_qkv_norm_rope(at::Tensor qkv, at::Tensor positions, at::Tensor q_weight,
                                at::Tensor k_weight, at::Tensor cos_sin_cache, int64_t num_q_heads,
@@ -248,6 +330,11 @@ TORCH_LIBRARY(custom_esimd_kernels_vllm, m) {
          &esimd_fused_add_rms_norm_batched_fp8);
   m.def("esimd_gelu_and_mul(Tensor input, Tensor output) -> Tensor");
   m.impl("esimd_gelu_and_mul", c10::DispatchKey::CUDA, &esimd_gelu_and_mul);
+  m.def("esimd_gemv_fp8_gelu_mul(Tensor input, Tensor weight, Tensor weight_scale, Tensor output) -> Tensor");
+  m.impl("esimd_gemv_fp8_gelu_mul", c10::DispatchKey::CUDA, &esimd_gemv_fp8_gelu_mul);
+  m.def("esimd_fused_add_rms_norm_gelu_mul_fp8(Tensor hidden_states, Tensor residual, Tensor weight, float eps, "
+        "Tensor qweight, Tensor qweight_scale, Tensor output) -> Tensor");
+  m.impl("esimd_fused_add_rms_norm_gelu_mul_fp8", c10::DispatchKey::CUDA, &esimd_fused_add_rms_norm_gelu_mul_fp8);
   m.def("esimd_qkv_norm_rope(Tensor qkv, Tensor positions, Tensor q_weight, Tensor k_weight, "
         "Tensor cos_sin_cache, int num_q_heads, int num_kv_heads, int head_dim, float eps, "
         "bool is_neox) -> Tensor");

@@ -100,6 +100,23 @@ def esimd_gelu_and_mul(input: torch.Tensor, output: torch.Tensor) -> torch.Tenso
     return _ops.esimd_gelu_and_mul(input, output)
 
 
+def esimd_gemv_fp8_gelu_mul(input: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
+                            output: torch.Tensor) -> torch.Tensor:
+    """output [M, N] = gelu_tanh(g) * u, [g | u] = GEMV(input, weight [2N, K] fp8 with gate rows
+    then up rows, weight_scale [2N] or scalar), each half rounded to the io dtype first: the
+    gate_up projection with GeLU-and-mul fused into its epilogue."""
+    return _ops.esimd_gemv_fp8_gelu_mul(input, weight, weight_scale, output)
+
+
+def esimd_fused_add_rms_norm_gelu_mul_fp8(hidden_states: torch.Tensor, residual: torch.Tensor,
+                                          weight: torch.Tensor, eps: float, qweight: torch.Tensor,
+                                          qweight_scale: torch.Tensor, output: torch.Tensor) -> torch.Tensor:
+    """esimd_fused_add_rms_norm_batched_fp8 with the gated projection of esimd_gemv_fp8_gelu_mul:
+    residual += hidden; output [M, N] = gelu(g) * u of GEMV(RMSNorm(residual) * weight, qweight [2N, K])."""
+    return _ops.esimd_fused_add_rms_norm_gelu_mul_fp8(hidden_states, residual, weight, eps, qweight,
+                                                      qweight_scale, output)
+
+
 def esimd_qkv_norm_rope(
     qkv: torch.Tensor, positions: torch.Tensor, q_weight: torch.Tensor,
     k_weight: torch.Tensor, cos_sin_cache: torch.Tensor,

@@ -72,6 +72,17 @@ CEK_API const char* cek_version(void);
  *           GEMV_fp8_pert_host  (csrc/xpu/esimd_kernels/fp8_GEMV_v2.h:414),
  *           GEMM_fp8_pert_dispatch, M <= 64 (csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4017). */
 #define CEK_GEMV_EARLY_WEIGHTS 1u
+/* flags |= CEK_GEMV_GELU_MUL_OUTPUT: gated output for the decode MLP's
+ * gate_up projection with GeLU-and-mul fused into its epilogue.  w holds 2N
+ * rows, the gate rows [0, N) then the up rows [N, 2N) (vLLM's merged
+ * gate_up layout); a per-N scale has 2N entries.  y is [M, N]:
+ *   y[m, n] = io( gelu_tanh(f32 g) * f32 u ),  g = io(GEMV row n),
+ *   u = io(GEMV row N + n),
+ * i.e. bit for bit the plain GEMV into [M, 2N] followed by cek_gelu_and_mul,
+ * in one launch and without the [M, 2N] round trip.  Supported for M <= 8
+ * and K % 64 == 0; otherwise CEK_ERR_UNSUPPORTED and nothing runs.  New: the
+ * reference has no GeLU op. */
+#define CEK_GEMV_GELU_MUL_OUTPUT 2u
 CEK_API int cek_gemv_fp8(const void* x, const void* w, const void* scale, void* y,
                          int64_t M, int64_t N, int64_t K, int x_dtype, int y_dtype,
                          int w_fmt, int scale_kind, unsigned flags, void* stream);
@@ -150,7 +161,9 @@ CEK_API int cek_fused_add_rmsnorm_gemv_fp8_noalloc(const void* hidden, void* res
 
 /* ---- GeLU(tanh)-and-mul ----------------------------------------------------
  * out[m, j] = gelu_tanh(x[m, j]) * x[m, d + j];  x: [M, 2d], out: [M, d].
- * d % 8 == 0.  No reference counterpart (vLLM's gelu_tanh_and_mul layout). */
+ * Any d >= 0 (d % 8 == 0: 16-byte vectors, x and out 16-byte aligned;
+ * otherwise element by element).  No reference counterpart (vLLM's
+ * gelu_tanh_and_mul layout). */
 CEK_API int cek_gelu_and_mul(const void* x, void* out, int64_t M, int64_t d, int dtype,
                      void* stream);
 

@@ -36,7 +36,7 @@ def _gemv(**kw):
 
 @pytest.mark.parametrize("kw", [
     dict(M=-1), dict(N=-1), dict(K=24), dict(xd=2), dict(yd=-1), dict(fmt=2), dict(sk=3),
-    dict(x=0), dict(w=0), dict(s=0), dict(y=0), dict(fl=2),
+    dict(x=0), dict(w=0), dict(s=0), dict(y=0), dict(fl=8),
 ])
 def test_gemv_rejects_bad_arguments(kw):
     assert _gemv(**kw) == cabi.CEK_ERR_INVALID_ARG
@@ -63,7 +63,7 @@ def test_norm_and_helpers_reject_bad_arguments():
     # workspace smaller than the inverse-RMS block
     assert L.cek_fused_add_rmsnorm_gemv_fp8(16, 16, 16, 1e-6, 16, 16, 16, 16, 8, 2, 64, 512, 0,
                                             0, 0, 0, None) == cabi.CEK_ERR_INVALID_ARG
-    assert L.cek_gelu_and_mul(16, 16, 1, 12, 0, None) == cabi.CEK_ERR_INVALID_ARG
+    assert L.cek_gelu_and_mul(16, 16, -1, 16, 0, None) == cabi.CEK_ERR_INVALID_ARG
     assert L.cek_gelu_and_mul(16, 16, 0, 16, 0, None) == cabi.CEK_OK
     assert L.cek_qkv_norm_rope(16, 16, 16, 16, 16, 1, 8, 1, 96, 64, 1e-6, 1, 0,
                                None) == cabi.CEK_ERR_INVALID_ARG

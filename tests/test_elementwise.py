@@ -9,7 +9,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("M,d", [(1, 28672), (16, 3584), (7, 8), (3, 1000)])
+@pytest.mark.parametrize("M,d", [(1, 28672), (16, 3584), (7, 8), (3, 1000), (2, 9), (4, 1500)])
 @pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
 def test_gelu_and_mul(ext, cuda_device, M, d, io):
     torch.manual_seed(0)
@@ -63,3 +63,90 @@ def test_quant_through_cabi(cuda_device):
     torch.cuda.synchronize()
     rq, rs = O.quant_fp8_per_token(a.cpu())
     assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
+
+
+# ---- GeLU-and-mul fused into the gate_up GEMV epilogue --------------------------
+
+def _gated_case(M, N, K, io, seed):
+    from esimd_learning_b200.workloads import make_fp8_weight
+    gen = torch.Generator().manual_seed(seed)
+    x = (torch.randn(M, K, generator=gen)).to(io)
+    wq, sc = make_fp8_weight(2 * N, K, gen)  # gate rows [0, N), up rows [N, 2N)
+    return x, wq, sc
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 512, 1024), (3, 1000, 4096), (8, 256, 2048), (1, 3584, 8192),
+                                   (2, 1500, 14336), (8, 4096, 8192), (5, 9, 64), (12, 256, 1024)])
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_gemv_gelu_mul(ext, cuda_device, M, N, K, io):
+    """The gated GEMV equals the plain GEMV into [M, 2N] followed by
+    esimd_gelu_and_mul, bit for bit (same GEMV sums, same rounding of gate
+    and up, same pinned GeLU arithmetic), for the fused kernel (M <= 8,
+    ragged N, K cut into pieces, x read from L2 at M = 8, K = 8192) and for
+    the op's two-launch fallback (M = 12).  Both agree with the oracle."""
+    import esimd_learning_b200 as ops
+
+    x, wq, sc = _gated_case(M, N, K, io, seed=M * 1000 + N)
+    xd, wd, sd = x.to(cuda_device), wq.to(cuda_device), sc.to(cuda_device)
+    y = torch.full((M, N), float("nan"), dtype=io, device=cuda_device)
+    ops.esimd_gemv_fp8_gelu_mul(xd, wd, sd, y)
+    gu = torch.empty(M, 2 * N, dtype=io, device=cuda_device)
+    ops.esimd_gemv_fp8_pern(xd, wd, sd, gu, 2 * N, K)
+    y2 = torch.empty(M, N, dtype=io, device=cuda_device)
+    ops.esimd_gelu_and_mul(gu, y2)
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+    O.assert_parity(y, O.gelu_and_mul(O.gemv_fp8(x, wq, sc)), f"M={M} N={N} K={K}")
+
+
+@pytest.mark.parametrize("M", [1, 4, 8, 16])
+def test_fused_norm_gelu_mul(ext, cuda_device, M):
+    """add + RMSNorm + gated gate_up GEMV + GeLU-and-mul equals the fused-norm
+    op into [M, 2N] followed by esimd_gelu_and_mul, bit for bit, including the
+    residual update (M = 16 takes the two-launch fallback)."""
+    import esimd_learning_b200 as ops
+    from esimd_learning_b200.workloads import make_fp8_weight
+
+    N, K = 1536, 4096
+    gen = torch.Generator().manual_seed(M)
+    h = torch.randn(M, K, generator=gen).half()
+    r = torch.randn(M, K, generator=gen).half()
+    gamma = (1 + 0.1 * torch.randn(K, generator=gen)).half()
+    wq, sc = make_fp8_weight(2 * N, K, gen)
+    dev = cuda_device
+    wd, sd, gd = wq.to(dev), sc.to(dev), gamma.to(dev)
+    h1, r1 = h.to(dev), r.to(dev)
+    y = torch.empty(M, N, dtype=torch.float16, device=dev)
+    ops.esimd_fused_add_rms_norm_gelu_mul_fp8(h1, r1, gd, 1e-6, wd, sd, y)
+    h2, r2 = h.to(dev), r.to(dev)
+    gu = torch.empty(M, 2 * N, dtype=torch.float16, device=dev)
+    ops.esimd_fused_add_rms_norm_batched_fp8(h2, r2, gd, 1e-6, wd, sd, gu)
+    y2 = torch.empty(M, N, dtype=torch.float16, device=dev)
+    ops.esimd_gelu_and_mul(gu, y2)
+    torch.cuda.synchronize()
+    assert torch.equal(r1, r2)
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+    ref_r, ref_n = O.add_rmsnorm(h, r, gamma, 1e-6)
+    O.assert_parity(y, O.gelu_and_mul(O.gemv_fp8(ref_n, wq, sc)), f"M={M}")
+
+
+def test_gelu_mul_output_flag_cabi(cuda_device):
+    """C ABI: CEK_GEMV_GELU_MUL_OUTPUT (N = output columns, w has 2N rows)
+    runs where the gated kernel fits and returns CEK_ERR_UNSUPPORTED,
+    launching nothing, where it does not (M > 8, K % 64 != 0)."""
+    x, wq, sc = _gated_case(2, 300, 4096, torch.float16, seed=5)
+    xd, wd, sd = x.to(cuda_device), wq.to(cuda_device), sc.to(cuda_device)
+    y = torch.zeros(2, 300, dtype=torch.float16, device=cuda_device)
+    cabi.call("cek_gemv_fp8", cabi.ptr(xd), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(y), 2, 300, 4096, cabi.CEK_F16,
+              cabi.CEK_F16, cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, cabi.CEK_GEMV_GELU_MUL_OUTPUT,
+              cabi.current_stream())
+    torch.cuda.synchronize()
+    O.assert_parity(y, O.gelu_and_mul(O.gemv_fp8(x, wq, sc)), "flag")
+    L = cabi.lib()
+    for M, K in ((12, 4096), (2, 4080)):
+        xb = torch.zeros(M, K, dtype=torch.float16, device=cuda_device)
+        yb = torch.zeros(M, 300, dtype=torch.float16, device=cuda_device)
+        rc = L.cek_gemv_fp8(cabi.ptr(xb), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(yb), M, 300, K, cabi.CEK_F16,
+                            cabi.CEK_F16, cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, cabi.CEK_GEMV_GELU_MUL_OUTPUT,
+                            cabi.current_stream())
+        assert rc == cabi.CEK_ERR_UNSUPPORTED

@@ -121,8 +121,11 @@ CEK_API int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* weig
  *      kernel writes xn there (M x K, L2-resident) and the GEMV reads it;
  *   >= 256 bytes only: the stats kernel writes the per-row inverse RMS and
  *      the GEMV forms xn inside its operand loads (slower).
- * flags: reserved for CEK_GEMV_EARLY_WEIGHTS (the weight stream always
- * starts early here: the stats kernel never writes w).
+ * flags: CEK_GEMV_EARLY_WEIGHTS is accepted and implied (the weight stream
+ * always starts early here: the stats kernel never writes w);
+ * CEK_GEMV_GELU_MUL_OUTPUT makes the projection the gated gate_up one of
+ * cek_gemv_fp8 (w [2N, K], y [M, N]); it needs the full workspace, M <= 8 and
+ * K % 64 == 0, else CEK_ERR_UNSUPPORTED before anything runs.
  * M <= 16, K % 8 == 0, K <= 16384.  No reference counterpart: the reference
  * runs fused_add_rms_norm_batched_host and GEMV_fp8_pern_host as two ops. */
 CEK_API int64_t cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(int64_t M, int64_t K);

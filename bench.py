@@ -332,7 +332,84 @@ def run_ours(args, rank, world, local):
         out["chain"] = measure_chain(dev, rank, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline_sample(seconds=args.cpu_seconds)
+    if rank == 0 and world == 1 and not args.no_vllm:
+        out["vllm"] = vllm_compare_subprocess()
     return out
+
+
+def vllm_compare_subprocess(timeout_s: int = 240) -> dict:
+    """Runs `bench.py --vllm-compare` in a child process (vLLM's import and
+    kernels must not be able to take this run down) and returns its JSON."""
+    import subprocess
+    try:
+        r = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--vllm-compare"], capture_output=True,
+                           text=True, timeout=timeout_s)
+        lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+        if r.returncode != 0 or not lines:
+            return {"unavailable": f"exit {r.returncode}: {(r.stderr or r.stdout).strip().splitlines()[-1:]}"}
+        return json.loads(lines[-1])
+    except Exception as e:  # noqa: BLE001 - a comparison, never fatal
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+
+
+def vllm_compare() -> dict:
+    """Config-1 shapes at M = 1 and 8: our W8A16 GEMV (fp16 activations, as
+    the reference ops) against vLLM 0.22's CUDA FP8 linear path on the same
+    weights, dynamic per-token activation quantisation (scaled_fp8_quant)
+    followed by cutlass_scaled_mm (W8A8).  Both timed as CUDA-graph replays
+    over rotating weight copies (> 320 MB per shape, cold L2), CUDA events."""
+    import esimd_learning_b200 as ops
+    from vllm import _custom_ops as vops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    res = {"vllm": __import__("vllm").__version__,
+           "path": "scaled_fp8_quant(per-token) + cutlass_scaled_mm, W8A8, fp16 out",
+           "ours": "esimd_gemv_fp8_pern, W8A16 (no activation quantisation)"}
+    st = torch.cuda.Stream(dev)
+
+    def graph_time(fn, copies, reps):
+        with torch.cuda.stream(st):
+            for c in copies:
+                fn(c)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                for r in range(reps):
+                    fn(copies[r % len(copies)])
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            g.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    for name, N, K in SHAPES:
+        ncopy = max(2, -(-(320 << 20) // (N * K)))
+        gen = torch.Generator(device=dev).manual_seed(7)
+        copies = [torch.randint(0, 120, (N, K), dtype=torch.uint8, device=dev, generator=gen)
+                  .view(torch.float8_e4m3fn) for _ in range(ncopy)]
+        sc = torch.rand(N, device=dev) * 0.01 + 1e-3
+        for M in (1, 8):
+            x = torch.randn(M, K, device=dev).half()
+            y = torch.empty(M, N, device=dev, dtype=torch.float16)
+            ours = graph_time(lambda w: ops.esimd_gemv_fp8_pern(x, w, sc, y, N, K), copies, 2 * ncopy)
+
+            def vllm_call(w):
+                xq, xs = vops.scaled_fp8_quant(x, use_per_token_if_dynamic=True)
+                return vops.cutlass_scaled_mm(xq, w.t(), scale_a=xs, scale_b=sc.view(-1, 1), out_dtype=torch.float16)
+
+            try:
+                theirs = graph_time(vllm_call, copies, 2 * ncopy)
+            except Exception as e:  # noqa: BLE001
+                theirs = f"{type(e).__name__}: {str(e)[:120]}"
+            res[f"{name}_M{M}"] = {"ours_us": round(ours, 2),
+                                   "vllm_us": round(theirs, 2) if isinstance(theirs, float) else theirs}
+        del copies
+        torch.cuda.empty_cache()
+    return res
 
 
 def measure_chain(dev, rank: int, world: int, Ms=(1, 8), reps: int = 200) -> dict:
@@ -610,6 +687,8 @@ def main():
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
     ap.add_argument("--no-chain", action="store_true", help="skip the config-4 decode-chain measurement")
     ap.add_argument("--no-prefetch", action="store_true", help="GEMVs wait for the previous kernel before any load")
+    ap.add_argument("--no-vllm", action="store_true", help="skip the vLLM FP8 linear comparison")
+    ap.add_argument("--vllm-compare", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--profile-chain", type=int, default=0, metavar="M",
                     help="run two eager TP=1 decode-chain steps (config 4) at this M and exit; for ncu")
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="M",
@@ -617,6 +696,9 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="run two eager config-1 steps (24 GEMV launches) and exit; for ncu captures")
     args = ap.parse_args()
+    if args.vllm_compare:
+        print(json.dumps(vllm_compare()), file=out_file, flush=True)
+        return
     if args.profile:
         profile_steps()
         return

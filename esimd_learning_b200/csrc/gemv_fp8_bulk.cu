@@ -64,6 +64,11 @@ constexpr int kSmemBudget = 216 * 1024;    // dynamic shared memory per CTA (sta
 constexpr uint32_t kWaitPolls = 1u << 22;
 constexpr int kXBatch = 8;                 // chunks per batch when x is read from global memory
 constexpr int kUnroll = 2;                 // chunk loop unroll when x is in shared memory
+// Where the consumers read x from: shared memory (copied once per CTA), L2,
+// or tensor memory (each consumer warp's chunks of x, stored once per CTA:
+// used when x does not fit in shared memory beside two slabs).
+constexpr int kXSmem = 0, kXL2 = 1, kXTmem = 2;
+constexpr int kTmemCols = 512;             // all of TMEM: 256 columns per consumer warp
 
 __device__ unsigned long long g_timeouts;
 #ifdef CEK_BULK_TRACE
@@ -77,7 +82,7 @@ CEK_DEVICE unsigned long long gtime() { unsigned long long t; asm volatile("mov.
 
 // x_bytes: x staged in shared memory; ks: bytes of a row per slab (K / pieces);
 // slab_bytes = 16 * ks.
-struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid; };  // x_bytes == 0: x read from global memory
+struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid, xmode; };
 
 // Row blocks over the rows of one matrix, or of up to kMaxMats matrices
 // sharing x (multi-GEMV, rows concatenated): a block is at most `bsz` rows
@@ -118,11 +123,12 @@ CEK_DEVICE int count_blocks(const GemvParams& p, int r0, int r1, int bsz) {
   return n;
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT, bool XG>
+template <typename InT, int FMT, int SCALE, typename OutT, int XM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], xbar;
+  __shared__ uint32_t tmem_base;
   __shared__ float red[2][kConsumers][kSlabRows][8];  // [row block parity][consumer][row][token]  // [row block parity][consumer][row][token]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -201,7 +207,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       for (int i = 0; i < pre; ++i) issue(i);
     pdl_wait();
     if (lane == 0) TRACE(tslot, 3);
-    if (!XG && lane == 0) {
+    if (XM == kXSmem && lane == 0) {
       const uint32_t xb = (uint32_t)p.M * (uint32_t)K * 2u;
       const uint32_t bar = mbar::saddr(&xbar);
       mbar::arrive_expect_tx(bar, xb);
@@ -239,6 +245,30 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   // slabs requested early, so until it lands the slabs use the global path.
   pdl_wait();
   bool x_smem = false;
+  // tensor-memory copy of x: warp cw owns global chunks cw, cw + 8, ...; its
+  // chunk j sits in columns [8j, 8j + 8) of its half of its lane quadrant
+  // (warps cw and cw + 4 share the quadrant of warp index % 4), lane (g, t)
+  // holding token g's 16 activations at k = 64 chunk + 16 t
+  uint32_t xt = 0;
+  if constexpr (XM == kXTmem) {
+    if (cw == 0) {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                   ::"r"(mbar::saddr(&tmem_base)), "r"(kTmemCols) : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    xt = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (cw >= 4 ? kTmemCols / 2 : 0);
+    for (int j = 0; cw + j * kConsumers < K / 64; ++j) {
+      const InT* xq = xglob + 64 * (cw + j * kConsumers);
+      const uint4 a = ldg_nc(xq), b = ldg_nc(xq + 8);
+      asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                   ::"r"(xt + 8u * j), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z),
+                   "r"(b.w) : "memory");
+    }
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  }
   if (cw == 0 && lane == 0) TRACE(tslot, 5);
 
   // one 64-k chunk: rows g, g+8 (16 bytes each) against 16 activations of token g
@@ -277,12 +307,34 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       dead = true;
       if (lane == 0) atomicAdd(&g_timeouts, 1ull);
     }
+    dead = __any_sync(0xffffffffu, dead);  // warp-uniform: the tensor-memory loads are warp-collective
     if (i == 0 && cw == 0 && lane == 0) TRACE(tslot, 7);
     const uint32_t wrow = mbar::saddr(smem + pl.x_bytes) + (uint32_t)s * pl.slab_bytes + (uint32_t)g * pl.pitch + 16u * t;
     const uint32_t wrow8 = wrow + 8u * pl.pitch;
-    if (!XG && !x_smem) x_smem = __shfl_sync(0xffffffffu, lane == 0 ? mbar::try_wait(mbar::saddr(&xbar), 0) : false, 0);
+    if (XM == kXSmem && !x_smem) x_smem = __shfl_sync(0xffffffffu, lane == 0 ? mbar::try_wait(mbar::saddr(&xbar), 0) : false, 0);
     if (!dead) {
-      if (x_smem) {
+      if constexpr (XM == kXTmem) {
+        // chunk c of piece pc is global chunk pc * nchunks + c, column 8 * (that / 8)
+        const uint32_t xcol = xt + 8u * (uint32_t)((pc * nchunks + cw) / kConsumers);
+        for (int c = cw; c < nchunks; c += 2 * kConsumers) {
+          uint32_t v[16];
+          const bool two = c + kConsumers < nchunks;
+          const uint32_t col = xcol + 8u * (uint32_t)((c - cw) / kConsumers);
+          asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                         "=r"(v[7]) : "r"(col));
+          if (two)
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                         : "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                           "=r"(v[14]), "=r"(v[15]) : "r"(col + 8u));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), make_uint4(v[0], v[1], v[2], v[3]),
+                    make_uint4(v[4], v[5], v[6], v[7]));
+          if (two)
+            chunk_mma(acc, mbar::lds16(wrow + 64u * (c + kConsumers)), mbar::lds16(wrow8 + 64u * (c + kConsumers)),
+                      make_uint4(v[8], v[9], v[10], v[11]), make_uint4(v[12], v[13], v[14], v[15]));
+        }
+      } else if (x_smem) {
         const uint32_t xpc = xrow + (uint32_t)pc * KS * 2u;
 #pragma unroll (kUnroll)
         for (int c = cw; c < nchunks; c += kConsumers)
@@ -353,8 +405,15 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       }
     }
   }
+  if constexpr (XM == kXTmem) {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (cw == 0)
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
   // the CTA's shared memory must outlive the x copy into it
-  if (!XG && !x_smem && cw == 0 && !mbar::wait(mbar::saddr(&xbar), 0, kWaitPolls) && lane == 0)
+  if (XM == kXSmem && !x_smem && cw == 0 && !mbar::wait(mbar::saddr(&xbar), 0, kWaitPolls) && lane == 0)
     atomicAdd(&g_timeouts, 1ull);
   if (cw == 0 && lane == 0) TRACE(tslot, 6);
 }
@@ -394,6 +453,14 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   if (M < 1 || M > 8 || K % 64 != 0 || K <= 0 || N <= 0 || K > (1 << 20)) return pl;
   const int64_t xb = ((M * K * 2) + 127) / 128 * 128;
   if (!try_plan(pl, xb, K, 3) && !try_plan(pl, xb, K, 2) && !try_plan(pl, 0, K, 3)) return Plan{};
+  pl.xmode = kXSmem;
+  if (pl.x_bytes == 0) {
+    // tensor memory holds 8 columns (one 64-k chunk of 16 activations per
+    // lane) per chunk a warp owns: K / 64 columns per warp, 256 available;
+    // chunk ownership (every 8th chunk) must not change across K pieces
+    const bool tmem_fits = K % 512 == 0 && K / 64 <= kTmemCols / 2 && (pl.ks / 64) % kConsumers == 0;
+    pl.xmode = tmem_fits ? kXTmem : kXL2;
+  }
   pl.smem = pl.x_bytes + pl.stages * pl.slab_bytes;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -402,9 +469,9 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   return pl;
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT, bool XG>
+template <typename InT, int FMT, int SCALE, typename OutT, int XM>
 int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
-  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XG>;
+  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM>;
   static int configured_smem[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -430,7 +497,9 @@ template <typename InT, typename OutT>
 int dispatch(const GemvParams& p, const Plan& pl, int w_fmt, int scale_kind, cudaStream_t st) {
 #define CEK_CASE(F, S) \
   if (w_fmt == F && scale_kind == S)                                    \
-    return pl.x_bytes ? launch<InT, F, S, OutT, false>(p, pl, st) : launch<InT, F, S, OutT, true>(p, pl, st);
+    return pl.xmode == kXSmem  ? launch<InT, F, S, OutT, kXSmem>(p, pl, st)            \
+           : pl.xmode == kXTmem ? launch<InT, F, S, OutT, kXTmem>(p, pl, st)           \
+                                : launch<InT, F, S, OutT, kXL2>(p, pl, st);
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERN_F16)
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERN_F32)
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERT_F32)

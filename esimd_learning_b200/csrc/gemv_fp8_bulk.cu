@@ -452,14 +452,27 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   Plan pl = {};
   if (M < 1 || M > 8 || K % 64 != 0 || K <= 0 || N <= 0 || K > (1 << 20)) return pl;
   const int64_t xb = ((M * K * 2) + 127) / 128 * 128;
-  if (!try_plan(pl, xb, K, 3) && !try_plan(pl, xb, K, 2) && !try_plan(pl, 0, K, 3)) return Plan{};
-  pl.xmode = kXSmem;
-  if (pl.x_bytes == 0) {
-    // tensor memory holds 8 columns (one 64-k chunk of 16 activations per
-    // lane) per chunk a warp owns: K / 64 columns per warp, 256 available;
-    // chunk ownership (every 8th chunk) must not change across K pieces
-    const bool tmem_fits = K % 512 == 0 && K / 64 <= kTmemCols / 2 && (pl.ks / 64) % kConsumers == 0;
-    pl.xmode = tmem_fits ? kXTmem : kXL2;
+  // x in shared memory with three slabs; else x in tensor memory (when its
+  // layout fits) with three slabs; else x in shared memory with two; else x
+  // from L2.  Tensor memory holds 8 columns (one 64-k chunk of 16
+  // activations per lane) per chunk a warp owns: K / 64 columns per warp,
+  // 256 available, and chunk ownership (every 8th chunk) must not change
+  // across K pieces.
+  auto tmem_fits = [&](const Plan& q) {
+    return K % 512 == 0 && K / 64 <= kTmemCols / 2 && (q.ks / 64) % kConsumers == 0;
+  };
+  Plan t = {};
+  if (try_plan(pl, xb, K, 3)) {
+    pl.xmode = kXSmem;
+  } else if (try_plan(t, 0, K, 3) && tmem_fits(t)) {
+    pl = t;
+    pl.xmode = kXTmem;
+  } else if (try_plan(pl, xb, K, 2)) {
+    pl.xmode = kXSmem;
+  } else if (try_plan(pl, 0, K, 3)) {
+    pl.xmode = kXL2;
+  } else {
+    return Plan{};
   }
   pl.smem = pl.x_bytes + pl.stages * pl.slab_bytes;
   int dev = 0, sms = 148;

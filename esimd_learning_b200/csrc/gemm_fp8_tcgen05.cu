@@ -38,9 +38,13 @@ namespace gemm {
 constexpr int BM = 128, BK = 128;  // BK in bytes: 128 e4m3 or 64 fp16/bf16 elements
 
 // Operand kinds: e4m3 x e4m3 (tcgen05 kind::f8f6f4), fp16 x fp16 and
-// bf16 x bf16 (kind::f16).  All K-major, fp32 accumulation.
-enum Kind { kE4M3 = 0, kF16 = 1, kBF16 = 2 };
-constexpr int THREADS = 6 * 32;
+// bf16 x bf16 (kind::f16), and fp16 / bf16 activations against FP8 weights
+// converted in shared memory (kF16W8 / kBF16W8: kind::f16 MMAs on the
+// converted tile).  All K-major, fp32 accumulation.
+enum Kind { kE4M3 = 0, kF16 = 1, kBF16 = 2, kF16W8 = 3, kBF16W8 = 4 };
+__host__ __device__ constexpr bool is_w8(int k) { return k == kF16W8 || k == kBF16W8; }
+// the kind whose MMA runs: W8 kinds multiply the converted 16-bit tile
+__host__ __device__ constexpr int mma_kind(int k) { return k == kF16W8 ? kF16 : k == kBF16W8 ? kBF16 : k; }
 constexpr int TMEM_COLS = 512;     // two accumulators of up to 256 fp32 columns
 constexpr int kSmemBudget = 227 * 1024;
 
@@ -48,12 +52,17 @@ constexpr int kSmemBudget = 227 * 1024;
 // stage count fills the shared-memory budget.
 template <int BN, int KIND>
 struct Tile {
-  static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
+  // W8 kinds add the FP8 staging tile (BN rows x 64 bytes) that the
+  // converter warps turn into the 16-bit B tile
+  static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, Q_BYTES = is_w8(KIND) ? BN * 64 : 0;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + Q_BYTES;
+  // warps: 0 TMA producer, 1 MMA, 2-5 epilogue, 6-9 converters (W8 kinds)
+  static constexpr int THREADS = (is_w8(KIND) ? 10 : 6) * 32;
   static constexpr int STAGES = (kSmemBudget - 2048) / STAGE_BYTES > 6 ? 6 : (kSmemBudget - 2048) / STAGE_BYTES;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
   // fp32 accumulate (bit 4), A/B format (bits 7-9 / 10-12: e4m3 = 0 for
   // kind::f8f6f4; f16 = 0, bf16 = 1 for kind::f16), both K-major, N = BN, M = 128
-  static constexpr uint32_t FMT = KIND == kBF16 ? 1u : 0u;
+  static constexpr uint32_t FMT = mma_kind(KIND) == kBF16 ? 1u : 0u;
   static constexpr uint32_t IDESC =
       (1u << 4) | (FMT << 7) | (FMT << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 };
@@ -150,15 +159,16 @@ struct Params {
   int b_scalar;
 };
 
-template <typename OutT, int BN, int KIND>
-__global__ void __launch_bounds__(THREADS, 1)
+template <typename OutT, int BN, int KIND, int WFMT = 0>
+__global__ void __launch_bounds__(Tile<BN, KIND>::THREADS, 1)
 gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const Params p) {
   using TL = Tile<BN, KIND>;
-  constexpr int STAGES = TL::STAGES, STAGE_BYTES = TL::STAGE_BYTES, A_BYTES = TL::A_BYTES;
+  constexpr int STAGES = TL::STAGES, STAGE_BYTES = TL::STAGE_BYTES, A_BYTES = TL::A_BYTES, B_BYTES = TL::B_BYTES;
+  constexpr bool W8 = is_w8(KIND);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
-  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES], conv_bar[STAGES];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -171,6 +181,7 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
     for (int s = 0; s < STAGES; ++s) {
       bar_init(saddr(&full_bar[s]), 1);
       bar_init(saddr(&empty_bar[s]), 1);
+      bar_init(saddr(&conv_bar[s]), 4);
     }
     for (int b = 0; b < 2; ++b) {
       bar_init(saddr(&acc_full[b]), 1);
@@ -203,9 +214,16 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           if (!wait(saddr(&empty_bar[s]), ((it / STAGES) & 1) ^ 1, &abort_flag)) break;
           uint8_t* sa = smem + s * STAGE_BYTES;
           const uint32_t fb = saddr(&full_bar[s]);
-          bar_expect_tx(fb, STAGE_BYTES);
-          tma_load_2d(saddr(sa), &map_a, kb * p.kblock_elems, mb * BM, fb);
-          tma_load_2d(saddr(sa + A_BYTES), &map_b, kb * p.kblock_elems, nb * BN, fb);
+          if constexpr (W8) {
+            // A (16-bit, swizzled) and the FP8 weight tile into the staging area
+            bar_expect_tx(fb, A_BYTES + TL::Q_BYTES);
+            tma_load_2d(saddr(sa), &map_a, kb * p.kblock_elems, mb * BM, fb);
+            tma_load_2d(saddr(sa + A_BYTES + B_BYTES), &map_b, kb * p.kblock_elems, nb * BN, fb);
+          } else {
+            bar_expect_tx(fb, STAGE_BYTES);
+            tma_load_2d(saddr(sa), &map_a, kb * p.kblock_elems, mb * BM, fb);
+            tma_load_2d(saddr(sa + A_BYTES), &map_b, kb * p.kblock_elems, nb * BN, fb);
+          }
         }
       }
       // Before leaving, make sure no copy of ours is still landing (bounded).
@@ -224,12 +242,14 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % STAGES;
-          if (!wait(saddr(&full_bar[s]), (it / STAGES) & 1, &abort_flag)) { ok = false; break; }
+          // W8: the converters' barrier (they waited for the copies first)
+          if (!wait(saddr(W8 ? &conv_bar[s] : &full_bar[s]), (it / STAGES) & 1, &abort_flag)) { ok = false; break; }
           fence_after();
           const uint32_t a0 = saddr(smem + s * STAGE_BYTES), b0 = a0 + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 32; ++k)
-            mma_issue<KIND>(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), TL::IDESC, (kb | k) ? 1u : 0u);
+            mma_issue<mma_kind(KIND)>(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), TL::IDESC,
+                                      (kb | k) ? 1u : 0u);
           mma_commit(saddr(&empty_bar[s]));
         }
         if (!ok) break;
@@ -238,6 +258,49 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       // All MMAs of this thread finished before TMEM is released (bounded).
       mma_commit(saddr(&drain_bar));
       wait(saddr(&drain_bar), 0, &abort_flag);
+    }
+  } else if (W8 && warp >= 6) {
+    // ---------------- converters (warps 6..9, W8 kinds) ----------------
+    // FP8 staging tile (BN rows x 64 bytes, dense) -> 16-bit B tile in the
+    // layout a 128-byte-swizzled TMA copy would leave: row r at 128 r, 16-byte
+    // chunk j at chunk position j ^ (r & 7).  Exact conversion.
+    const int ct = threadIdx.x - 6 * 32;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles && !abort_flag; t += gridDim.x) {
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!wait(saddr(&full_bar[s]), (it / STAGES) & 1, &abort_flag)) { ok = false; break; }
+        const uint32_t bt = saddr(smem + s * STAGE_BYTES) + A_BYTES, qt = bt + B_BYTES;
+        for (int u = ct; u < BN * 2; u += 128) {
+          const int r = u >> 1, h = u & 1;
+          uint4 q[2];
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(q[0].x), "=r"(q[0].y), "=r"(q[0].z), "=r"(q[0].w)
+                       : "r"(qt + r * 64 + h * 32));
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(q[1].x), "=r"(q[1].y), "=r"(q[1].z), "=r"(q[1].w)
+                       : "r"(qt + r * 64 + h * 32 + 16));
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t w0 = (c & 1) ? q[c >> 1].z : q[c >> 1].x, w1 = (c & 1) ? q[c >> 1].w : q[c >> 1].y;
+            uint32_t o[4];
+            if constexpr (mma_kind(KIND) == kF16) {
+              o[0] = fp8x2_to_f16x2<WFMT, 0>(w0); o[1] = fp8x2_to_f16x2<WFMT, 1>(w0);
+              o[2] = fp8x2_to_f16x2<WFMT, 0>(w1); o[3] = fp8x2_to_f16x2<WFMT, 1>(w1);
+            } else {
+              o[0] = fp8x2_to_bf16x2<WFMT, 0>(w0); o[1] = fp8x2_to_bf16x2<WFMT, 1>(w0);
+              o[2] = fp8x2_to_bf16x2<WFMT, 0>(w1); o[3] = fp8x2_to_bf16x2<WFMT, 1>(w1);
+            }
+            const int j = 4 * h + c;
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(bt + r * 128 + ((j ^ (r & 7)) << 4)),
+                         "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]) : "memory");
+          }
+        }
+        // the tensor cores read shared memory through the async proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) bar_arrive(saddr(&conv_bar[s]));
+      }
+      if (!ok) break;
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
@@ -310,23 +373,26 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Row-major [rows, cols] matrix of `eb`-byte elements; box = one 128-byte
-// k-block x box_rows rows (box_rows <= 256, the TMA box limit).
-bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int eb = 1) {
+// Row-major [rows, cols] matrix of `eb`-byte elements; box = box_bytes of a
+// row (one k-block) x box_rows rows (box_rows <= 256, the TMA box limit),
+// 128-byte swizzle unless `dense` (the W8 staging tile).
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int eb = 1,
+              int box_bytes = BK, bool dense = false) {
   auto enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(cols * eb)};
-  cuuint32_t box[2] = {(cuuint32_t)(BK / eb), (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)(box_bytes / eb), (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
-  return enc(m, eb == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, es,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  return enc(m, eb == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base),
+             dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             dense ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename OutT, int BN, int KIND>
+template <typename OutT, int BN, int KIND, int WFMT = 0>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t st) {
-  auto kern = gemm_fp8_kernel<OutT, BN, KIND>;
+  auto kern = gemm_fp8_kernel<OutT, BN, KIND, WFMT>;
   constexpr int SMEM_BYTES = Tile<BN, KIND>::SMEM_BYTES;
   static unsigned attr_set = 0;
   int dev = 0, sms = 148;
@@ -341,7 +407,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaSt
   const int tiles = p.num_m * p.num_n;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(tiles < sms ? tiles : sms));
-  cfg.blockDim = dim3(THREADS);
+  cfg.blockDim = dim3(Tile<BN, KIND>::THREADS);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -378,12 +444,15 @@ int choose_bn(int64_t M, int64_t N) {
 }
 
 // Builds the maps and launches: a [M, K] and b [N, K], elements of `eb` bytes.
-template <int KIND>
+template <int KIND, int WFMT = 0>
 int run(const void* a, const void* b, const float* a_scale, const float* b_scale, bool b_scalar, void* y,
         int64_t M, int64_t N, int64_t K, int eb, int y_dtype, cudaStream_t st) {
   const int bn = choose_bn(M, N);
   CUtensorMap ma, mb;
-  if (!make_map(&ma, a, M, K, BM, eb) || !make_map(&mb, b, N, K, bn, eb)) return CEK_ERR_LAUNCH;
+  // W8 kinds: b is the FP8 weight, copied as dense 64-byte x bn boxes (one
+  // k-block of 64 elements) into the staging tile
+  const bool bmap = is_w8(KIND) ? make_map(&mb, b, N, K, bn, 1, 64, true) : make_map(&mb, b, N, K, bn, eb);
+  if (!make_map(&ma, a, M, K, BM, eb) || !bmap) return CEK_ERR_LAUNCH;
   Params p;
   p.a_scale = a_scale; p.b_scale = b_scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
@@ -393,8 +462,8 @@ int run(const void* a, const void* b, const float* a_scale, const float* b_scale
   p.kblock_elems = BK / eb;
   p.b_scalar = b_scalar ? 1 : 0;
 #define CEK_GEMM_BN(B)                                                                        \
-  if (bn == B) return y_dtype == CEK_F16 ? launch<__half, B, KIND>(ma, mb, p, st)            \
-                                         : launch<__nv_bfloat16, B, KIND>(ma, mb, p, st);
+  if (bn == B) return y_dtype == CEK_F16 ? launch<__half, B, KIND, WFMT>(ma, mb, p, st)      \
+                                         : launch<__nv_bfloat16, B, KIND, WFMT>(ma, mb, p, st);
   CEK_GEMM_BN(256) CEK_GEMM_BN(224) CEK_GEMM_BN(192) CEK_GEMM_BN(160)
 #undef CEK_GEMM_BN
   return CEK_ERR_UNSUPPORTED;
@@ -446,6 +515,14 @@ extern "C" int64_t cek_gemm_fp8w_workspace_bytes(int64_t N, int64_t K) {
   return ((N * K * 2 + 255) / 256) * 256;
 }
 
+// Up to this many tokens the weight tile is converted inside the GEMM (each
+// tile once per 128-row block: cheap while there are few); above it the
+// weight is dequantised once into the workspace and the plain 16-bit GEMM
+// runs.  Measured at N = 14336, K = 4096: in-kernel 34.9 / 46.6 / 86.0 us at
+// M = 128 / 256 / 512 against 61.9 / 64.7 / 87.2 us dequantise-first, and
+// 283 against 206 us at M = 2048.
+constexpr int64_t kGemmW8MaxRows = 256;
+
 extern "C" int cek_gemm_fp8w(const void* x, const void* w, const void* scale, void* y, void* workspace,
                              int64_t workspace_bytes, int64_t M, int64_t N, int64_t K, int dtype, int w_fmt,
                              int scale_kind, void* stream) {
@@ -463,6 +540,15 @@ extern "C" int cek_gemm_fp8w(const void* x, const void* w, const void* scale, vo
       !cek_host::aligned16(workspace))
     return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float* sc = static_cast<const float*>(scale);
+  const bool scalar = scale_kind == CEK_SCALE_PERT_F32;
+  if (M <= kGemmW8MaxRows) {
+    if (dtype == CEK_F16)
+      return w_fmt == CEK_E4M3 ? run<kF16W8, CEK_E4M3>(x, w, nullptr, sc, scalar, y, M, N, K, 2, dtype, st)
+                               : run<kF16W8, CEK_E5M2>(x, w, nullptr, sc, scalar, y, M, N, K, 2, dtype, st);
+    return w_fmt == CEK_E4M3 ? run<kBF16W8, CEK_E4M3>(x, w, nullptr, sc, scalar, y, M, N, K, 2, dtype, st)
+                             : run<kBF16W8, CEK_E5M2>(x, w, nullptr, sc, scalar, y, M, N, K, 2, dtype, st);
+  }
   const int64_t n8 = N * K / 8;
   const unsigned blocks = (unsigned)((n8 + 255) / 256);
   const uint8_t* wq = static_cast<const uint8_t*>(w);
@@ -474,8 +560,6 @@ extern "C" int cek_gemm_fp8w(const void* x, const void* w, const void* scale, vo
   }
 #undef CEK_DQ
   if (cudaGetLastError() != cudaSuccess) return CEK_ERR_LAUNCH;
-  const float* sc = static_cast<const float*>(scale);
-  const bool scalar = scale_kind == CEK_SCALE_PERT_F32;
   return dtype == CEK_F16
              ? run<kF16>(x, workspace, nullptr, sc, scalar, y, M, N, K, 2, dtype, st)
              : run<kBF16>(x, workspace, nullptr, sc, scalar, y, M, N, K, 2, dtype, st);

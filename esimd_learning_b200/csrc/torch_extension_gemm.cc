@@ -12,8 +12,9 @@ using namespace cek_torch;
 // esimd_kernel_gemm.sycl:45-48,61-63).  Decode sizes (M <= 64) run the
 // tensor-core GEMV family: one weight pass per 16-token tile, the tiles of
 // one row group scheduled next to each other so re-reads hit L2.  Prefill
-// sizes (M > 64, K % 64 == 0, N % 16 == 0) dequantise the weight exactly into
-// a 16-bit workspace and run the tcgen05 GEMM (cek_gemm_fp8w).
+// sizes (M > 64, K % 64 == 0, N % 16 == 0) run the tcgen05 GEMM with the
+// weight converted exactly to 16 bits (cek_gemm_fp8w: in shared memory up to
+// 256 tokens, into a workspace first above that).
 // Token count above which the per-tensor GEMM leaves the GEMV family for the
 // tcgen05 GEMM (the reference's own decode/prefill split,
 // csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4043-4048).

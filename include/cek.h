@@ -238,10 +238,13 @@ CEK_API int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* a_s
  * Replaces the prefill branch of the reference's esimd_gemm_fp8_pert
  * (csrc/xpu/esimd_kernel_gemm.sycl:23-64 -> GEMM_fp8_pert_dispatch,
  * csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4043-4048, M > 64).
- * w is first dequantised exactly (every e4m3/e5m2 value is a 16-bit float
- * of dtype) into `workspace` (cek_gemm_fp8w_workspace_bytes(N, K) bytes),
- * then one kind::f16 tcgen05 GEMM with fp32 accumulation runs; the scale
+ * Exact weight conversion (every e4m3/e5m2 value is a 16-bit float of
+ * dtype), then kind::f16 tcgen05 MMAs with fp32 accumulation; the scale
  * (fp32 per-tensor scalar, or fp32 per-N) is applied in the epilogue.
+ * M <= 256: each weight tile is copied to shared memory as FP8 and
+ * converted there by converter warps (workspace untouched).  M > 256: the
+ * weight is dequantised once into `workspace`
+ * (cek_gemm_fp8w_workspace_bytes(N, K) bytes), then the 16-bit GEMM runs.
  * x, y, T = dtype (CEK_F16 / CEK_BF16), row-major and contiguous.
  * K % 64 == 0 and N % 16 == 0; x, w, y, workspace 16-byte aligned. */
 CEK_API int64_t cek_gemm_fp8w_workspace_bytes(int64_t N, int64_t K);

@@ -70,27 +70,36 @@ def test_gemm_pert_prefill_config3(ext, cuda_device):
 
 
 def test_gemm_fp8w_cabi_pern(cuda_device):
-    """C ABI with a per-N fp32 scale, bf16 I/O; workspace size rule and shape checks."""
-    M, N, K = 200, 272, 320
+    """C ABI with a per-N fp32 scale, bf16 I/O, e4m3 and e5m2 weights, at a
+    small M (weight tiles converted in shared memory) and a large one
+    (dequantised into the workspace first); workspace size rule; shape
+    checks."""
+    N, K = 272, 320
     torch.manual_seed(3)
-    w = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(torch.float8_e4m3fn)
-    sc = torch.rand(N) * 0.1 + 0.01
-    x = (torch.randn(M, K) * 0.1).bfloat16()
     L = cabi.lib()
     nb = L.cek_gemm_fp8w_workspace_bytes(N, K)
     assert nb >= N * K * 2 and nb % 256 == 0
     ws = torch.empty(nb, dtype=torch.uint8, device=cuda_device)
-    wd, sd, xd = w.to(cuda_device), sc.to(cuda_device), x.to(cuda_device)
-    y = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda_device)
-    cabi.call("cek_gemm_fp8w", cabi.ptr(xd), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(y), cabi.ptr(ws), nb,
-              M, N, K, cabi.CEK_BF16, cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, cabi.current_stream())
-    torch.cuda.synchronize()
-    O.assert_parity(y, O.gemv_fp8(x, w, sc), "fp8w cabi pern")
-    args = (cabi.ptr(xd), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(y), cabi.ptr(ws))
-    assert L.cek_gemm_fp8w(*args, nb - 256, M, N, K, cabi.CEK_BF16, cabi.CEK_E4M3,
+    for M, wdt in ((200, torch.float8_e4m3fn), (200, torch.float8_e5m2), (300, torch.float8_e5m2)):
+        w = (torch.randn(N, K, dtype=torch.float16) * 0.1).to(wdt)
+        sc = torch.rand(N) * 0.1 + 0.01
+        x = (torch.randn(M, K) * 0.1).bfloat16()
+        wd, sd, xd = w.to(cuda_device), sc.to(cuda_device), x.to(cuda_device)
+        y = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda_device)
+        cabi.call("cek_gemm_fp8w", cabi.ptr(xd), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(y), cabi.ptr(ws), nb,
+                  M, N, K, cabi.CEK_BF16, cabi.fp8_format(wd), cabi.CEK_SCALE_PERN_F32, cabi.current_stream())
+        torch.cuda.synchronize()
+        O.assert_parity(y, O.gemv_fp8(x, w, sc), f"fp8w cabi pern M={M} {wdt}")
+    args = (cabi.ptr(xd), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(y), cabi.ptr(ws), nb)
+    assert L.cek_gemm_fp8w(cabi.ptr(xd), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(y), cabi.ptr(ws), nb - 256, M, N, K,
+                           cabi.CEK_BF16, cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, None) == cabi.CEK_ERR_INVALID_ARG
+    assert L.cek_gemm_fp8w(*args, M, N, 96, cabi.CEK_BF16, cabi.CEK_E4M3,
                            cabi.CEK_SCALE_PERN_F32, None) == cabi.CEK_ERR_INVALID_ARG
-    assert L.cek_gemm_fp8w(*args, nb, M, N, 96, cabi.CEK_BF16, cabi.CEK_E4M3,
+    assert L.cek_gemm_fp8w(*args, M, 250, K, cabi.CEK_BF16, cabi.CEK_E4M3,
                            cabi.CEK_SCALE_PERN_F32, None) == cabi.CEK_ERR_INVALID_ARG
+    n = __import__("ctypes").c_uint64(99)
+    cabi.call("cek_gemm_fp8_timeouts", __import__("ctypes").byref(n))
+    assert n.value == 0
 
 
 def test_gemm_vs_gemv_m1(ext, cuda_device):

@@ -14,7 +14,7 @@ One step, on every rank (rank r of TP):
    += attention output (given as an input), RMSNorm, the gate_up GEMV over
    this rank's [gate | up] rows (column-parallel, 57344 / TP rows) with
 4. GeLU(tanh)-and-mul in its epilogue: the local activation [M, 28672 / TP]
-   in one launch of the gated bulk GEMV (M > 8: the GEMV, then
+   in one launch of the gated bulk GEMV (M > 16: the GEMV, then
    ``esimd_gelu_and_mul``).
 5. The down GEMV on this rank's K-slice of the down weight (row-parallel,
    K = 28672 / TP) with the full per-channel scale: a partial sum of the

@@ -127,7 +127,7 @@ CEK_DEVICE void load_x16(const GemvParams& p, int tok, int k, uint32_t (&xw)[8])
   }
 }
 
-// Bulk-copy GEMV for up to 8 tokens (gemv_fp8_bulk.cu); CEK_ERR_UNSUPPORTED
+// Bulk-copy GEMV for up to 16 tokens (gemv_fp8_bulk.cu); CEK_ERR_UNSUPPORTED
 // when the call does not fit it.
 int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, int scale_kind, cudaStream_t st);
 

@@ -1,10 +1,10 @@
-// gemv_fp8_bulk.cu — the decode GEMV (M <= 8) as a bulk-copy stream.
+// gemv_fp8_bulk.cu — the decode GEMV (M <= 16) as a bulk-copy stream.
 //
 //   y[m, n] = OutT( sum_k x[m, k] * deq(w[n, k]) * scale(n) )
 //
 // Same contract as the split-K kernel in gemv_fp8.cu (the reference's
 // GEMV_fp8_pern_kernel / GEMV_fp8_pert_kernel, csrc/xpu/esimd_kernels/
-// fp8_GEMV_v2.h:44-90, 322-368); this is the path for up to 8 tokens and
+// fp8_GEMV_v2.h:44-90, 322-368); this is the path for up to 16 tokens and
 // K % 64 == 0.
 //
 // Why a second kernel.  With register-held weights every warp spends the
@@ -82,7 +82,7 @@ CEK_DEVICE unsigned long long gtime() { unsigned long long t; asm volatile("mov.
 
 // x_bytes: x staged in shared memory; ks: bytes of a row per slab (K / pieces);
 // slab_bytes = 16 * ks.
-struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid, xmode; };
+struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid, xmode, nt; };
 
 // Row blocks over the rows of one matrix, or of up to kMaxMats matrices
 // sharing x (multi-GEMV, rows concatenated): a block is at most `bsz` rows
@@ -123,13 +123,14 @@ CEK_DEVICE int count_blocks(const GemvParams& p, int r0, int r1, int bsz) {
   return n;
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT, int XM>
+// NT: 8-token groups (the n8 columns of the MMA), 1 for M <= 8, 2 for M <= 16.
+template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT>
 __global__ void __launch_bounds__(kThreads, 1)
 gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], xbar;
   __shared__ uint32_t tmem_base;
-  __shared__ float red[2][kConsumers][kSlabRows][8];  // [row block parity][consumer][row][token]  // [row block parity][consumer][row][token]
+  __shared__ float red[2][kConsumers][kSlabRows][8 * NT];  // [row block parity][consumer][row][token]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = p.K, KS = pl.ks, P = pl.pieces;
@@ -234,10 +235,16 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   // ---- consumers ----
   const int cw = warp - 1, g = lane >> 2, t = lane & 3;
   const int ctid = threadIdx.x - 32;
-  // Tokens >= M read token 0's activations: their output columns are never stored.
-  const int xtok = g < p.M ? g : 0;
-  const uint32_t xrow = mbar::saddr(smem) + (uint32_t)xtok * K * 2u + 32u * t;
-  const InT* xglob = reinterpret_cast<const InT*>(p.x) + (size_t)xtok * K + 16 * t;
+  // Lane (g, t) carries tokens g + 8u of the NT groups.  Tokens >= M read
+  // token 0's activations: their output columns are never stored.
+  uint32_t xrow[NT];
+  const InT* xglob[NT];
+#pragma unroll
+  for (int u = 0; u < NT; ++u) {
+    const int xtok = g + 8 * u < p.M ? g + 8 * u : 0;
+    xrow[u] = mbar::saddr(smem) + (uint32_t)xtok * K * 2u + 32u * t;
+    xglob[u] = reinterpret_cast<const InT*>(p.x) + (size_t)xtok * K + 16 * t;
+  }
   const int nchunks = KS / 64;
   bool dead = false;
   // x may be read from global memory (L2) only after the previous kernel
@@ -246,9 +253,10 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   pdl_wait();
   bool x_smem = false;
   // tensor-memory copy of x: warp cw owns global chunks cw, cw + 8, ...; its
-  // chunk j sits in columns [8j, 8j + 8) of its half of its lane quadrant
-  // (warps cw and cw + 4 share the quadrant of warp index % 4), lane (g, t)
-  // holding token g's 16 activations at k = 64 chunk + 16 t
+  // chunk j sits in columns [8 NT j, 8 NT (j + 1)) of its half of its lane
+  // quadrant (warps cw and cw + 4 share the quadrant of warp index % 4),
+  // lane (g, t) holding, per token group u, token g + 8u's 16 activations at
+  // k = 64 chunk + 16 t in columns 8 NT j + 8u ..
   uint32_t xt = 0;
   if constexpr (XM == kXTmem) {
     if (cw == 0) {
@@ -261,29 +269,38 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     xt = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (cw >= 4 ? kTmemCols / 2 : 0);
     for (int j = 0; cw + j * kConsumers < K / 64; ++j) {
-      const InT* xq = xglob + 64 * (cw + j * kConsumers);
-      const uint4 a = ldg_nc(xq), b = ldg_nc(xq + 8);
-      asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
-                   ::"r"(xt + 8u * j), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z),
-                   "r"(b.w) : "memory");
+#pragma unroll
+      for (int u = 0; u < NT; ++u) {
+        const InT* xq = xglob[u] + 64 * (cw + j * kConsumers);
+        const uint4 a = ldg_nc(xq), b = ldg_nc(xq + 8);
+        asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                     ::"r"(xt + 8u * (NT * j + u)), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y),
+                     "r"(b.z), "r"(b.w) : "memory");
+      }
     }
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
   }
   if (cw == 0 && lane == 0) TRACE(tslot, 5);
 
-  // one 64-k chunk: rows g, g+8 (16 bytes each) against 16 activations of token g
-  auto chunk_mma = [&](float (&ac)[kAcc][4], const uint4& wa, const uint4& wb, const uint4& xa, const uint4& xb) {
+  // one 64-k chunk: rows g, g+8 (16 bytes each) against the 16 activations
+  // of each token group (xa[u], xb[u]); the FP8 conversion is done once
+  auto chunk_mma = [&](float (&ac)[NT][kAcc][4], const uint4& wa, const uint4& wb, const uint4 (&xa)[NT],
+                       const uint4 (&xb)[NT]) {
     const uint32_t ra[4] = {wa.x, wa.y, wa.z, wa.w}, rb4[4] = {wb.x, wb.y, wb.z, wb.w};
-    const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint32_t a[4] = {cvt_pair<InT, FMT, 0>(ra[q]), cvt_pair<InT, FMT, 0>(rb4[q]),
                              cvt_pair<InT, FMT, 1>(ra[q]), cvt_pair<InT, FMT, 1>(rb4[q])};
-      mma16816<InT>(ac[q % kAcc], a, xw[2 * q], xw[2 * q + 1]);
+#pragma unroll
+      for (int u = 0; u < NT; ++u) {
+        const uint32_t b0 = (q < 2) ? ((q == 0) ? xa[u].x : xa[u].z) : ((q == 2) ? xb[u].x : xb[u].z);
+        const uint32_t b1 = (q < 2) ? ((q == 0) ? xa[u].y : xa[u].w) : ((q == 2) ? xb[u].y : xb[u].w);
+        mma16816<InT>(ac[u][q % kAcc], a, b0, b1);
+      }
     }
   };
 
-  float acc[kAcc][4];
+  float acc[NT][kAcc][4];
   float out_scale = 0.f, out_scale_up = 0.f;
   int out_row = 0;  // row inside the block's matrix of this thread's output
   bool out_ok = false;
@@ -297,9 +314,11 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       // now, so the load's latency hides behind the block's math
       cur.next(p, bm, brow, brows);
 #pragma unroll
-      for (int a = 0; a < kAcc; ++a) acc[a][0] = acc[a][1] = acc[a][2] = acc[a][3] = 0.f;
+      for (int u = 0; u < NT; ++u)
+#pragma unroll
+        for (int a = 0; a < kAcc; ++a) acc[u][a][0] = acc[u][a][1] = acc[u][a][2] = acc[u][a][3] = 0.f;
       out_row = brow + (ctid % bsz);
-      out_ok = ctid < bsz * 8 && (ctid % bsz) < brows;
+      out_ok = ctid < bsz * 8 * NT && (ctid % bsz) < brows;
       out_scale = out_ok ? load_scale<SCALE>(p.nmat ? p.mscales[bm] : p.scale, out_row) : 0.f;
       if (p.y_gelu) out_scale_up = out_ok ? load_scale<SCALE>(p.scale, p.N + out_row) : 0.f;
     }
@@ -314,48 +333,61 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     if (XM == kXSmem && !x_smem) x_smem = __shfl_sync(0xffffffffu, lane == 0 ? mbar::try_wait(mbar::saddr(&xbar), 0) : false, 0);
     if (!dead) {
       if constexpr (XM == kXTmem) {
-        // chunk c of piece pc is global chunk pc * nchunks + c, column 8 * (that / 8)
-        const uint32_t xcol = xt + 8u * (uint32_t)((pc * nchunks + cw) / kConsumers);
+        // chunk c of piece pc is global chunk pc * nchunks + c, the warp's
+        // chunk (that / 8), columns 8 NT (that / 8) + 8u
+        const uint32_t xcol = xt + 8u * NT * (uint32_t)((pc * nchunks + cw) / kConsumers);
         for (int c = cw; c < nchunks; c += 2 * kConsumers) {
-          uint32_t v[16];
+          // two chunks per tensor-memory wait
           const bool two = c + kConsumers < nchunks;
-          const uint32_t col = xcol + 8u * (uint32_t)((c - cw) / kConsumers);
-          asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                         "=r"(v[7]) : "r"(col));
-          if (two)
-            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                         : "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-                           "=r"(v[14]), "=r"(v[15]) : "r"(col + 8u));
+          const uint32_t col = xcol + 8u * NT * (uint32_t)((c - cw) / kConsumers);
+          uint4 xa[2][NT], xb[2][NT];
+#pragma unroll
+          for (int v = 0; v < 2; ++v)
+#pragma unroll
+            for (int u = 0; u < NT; ++u)
+              if (v == 0 || two)
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                             : "=r"(xa[v][u].x), "=r"(xa[v][u].y), "=r"(xa[v][u].z), "=r"(xa[v][u].w),
+                               "=r"(xb[v][u].x), "=r"(xb[v][u].y), "=r"(xb[v][u].z), "=r"(xb[v][u].w)
+                             : "r"(col + 8u * (NT * v + u)));
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), make_uint4(v[0], v[1], v[2], v[3]),
-                    make_uint4(v[4], v[5], v[6], v[7]));
+          chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), xa[0], xb[0]);
           if (two)
             chunk_mma(acc, mbar::lds16(wrow + 64u * (c + kConsumers)), mbar::lds16(wrow8 + 64u * (c + kConsumers)),
-                      make_uint4(v[8], v[9], v[10], v[11]), make_uint4(v[12], v[13], v[14], v[15]));
+                      xa[1], xb[1]);
         }
       } else if (x_smem) {
-        const uint32_t xpc = xrow + (uint32_t)pc * KS * 2u;
 #pragma unroll (kUnroll)
-        for (int c = cw; c < nchunks; c += kConsumers)
-          chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), mbar::lds16(xpc + 128u * c),
-                    mbar::lds16(xpc + 128u * c + 16u));
-      } else {
-        // x from L2: a batch of kXBatch chunks issues all its activation
-        // loads before the first MMA
-        const InT* xpc = xglob + (size_t)pc * KS;
-        for (int c0 = cw; c0 < nchunks; c0 += kXBatch * kConsumers) {
-          uint4 xa[kXBatch], xb[kXBatch];
+        for (int c = cw; c < nchunks; c += kConsumers) {
+          uint4 xa[NT], xb[NT];
 #pragma unroll
-          for (int u = 0; u < kXBatch; ++u) {
-            const int c = min(c0 + u * kConsumers, nchunks - 1);
-            xa[u] = ldg_nc(xpc + 64 * c);
-            xb[u] = ldg_nc(xpc + 64 * c + 8);
+          for (int u = 0; u < NT; ++u) {
+            const uint32_t xq = xrow[u] + (uint32_t)pc * KS * 2u + 128u * c;
+            xa[u] = mbar::lds16(xq);
+            xb[u] = mbar::lds16(xq + 16u);
+          }
+          chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), xa, xb);
+        }
+      } else {
+        // x from L2: a batch of kXBatch / NT chunks issues all its activation
+        // loads before the first MMA
+        constexpr int XB = kXBatch / NT;
+        for (int c0 = cw; c0 < nchunks; c0 += XB * kConsumers) {
+          uint4 xa[XB][NT], xb[XB][NT];
+#pragma unroll
+          for (int v = 0; v < XB; ++v) {
+            const int c = min(c0 + v * kConsumers, nchunks - 1);
+#pragma unroll
+            for (int u = 0; u < NT; ++u) {
+              const InT* xq = xglob[u] + (size_t)pc * KS + 64 * c;
+              xa[v][u] = ldg_nc(xq);
+              xb[v][u] = ldg_nc(xq + 8);
+            }
           }
 #pragma unroll
-          for (int u = 0; u < kXBatch; ++u) {
-            const int c = c0 + u * kConsumers;
-            if (c < nchunks) chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), xa[u], xb[u]);
+          for (int v = 0; v < XB; ++v) {
+            const int c = c0 + v * kConsumers;
+            if (c < nchunks) chunk_mma(acc, mbar::lds16(wrow + 64u * c), mbar::lds16(wrow8 + 64u * c), xa[v], xb[v]);
           }
         }
       }
@@ -363,19 +395,22 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     __syncwarp();
     if (lane == 0) mbar::arrive(mbar::saddr(&empty[s]));
     if (pc != P - 1) continue;
-    float v4[4] = {acc[0][0], acc[0][1], acc[0][2], acc[0][3]};
+    float (&rd)[kConsumers][kSlabRows][8 * NT] = red[rb & 1];
 #pragma unroll
-    for (int a = 1; a < kAcc; ++a)
+    for (int u = 0; u < NT; ++u) {
+      float v4[4] = {acc[u][0][0], acc[u][0][1], acc[u][0][2], acc[u][0][3]};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v4[e] += acc[a][e];
-    float (&rd)[kConsumers][kSlabRows][8] = red[rb & 1];
-    // v4[0..1]: block row g, tokens 2t, 2t+1; v4[2..3]: row g + 8
-    rd[cw][g][2 * t] = v4[0];
-    rd[cw][g][2 * t + 1] = v4[1];
-    rd[cw][g + 8][2 * t] = v4[2];
-    rd[cw][g + 8][2 * t + 1] = v4[3];
+      for (int a = 1; a < kAcc; ++a)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v4[e] += acc[u][a][e];
+      // v4[0..1]: block row g, tokens 8u + 2t, 8u + 2t + 1; v4[2..3]: row g + 8
+      rd[cw][g][8 * u + 2 * t] = v4[0];
+      rd[cw][g][8 * u + 2 * t + 1] = v4[1];
+      rd[cw][g + 8][8 * u + 2 * t] = v4[2];
+      rd[cw][g + 8][8 * u + 2 * t + 1] = v4[3];
+    }
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
-    if (ctid < bsz * 8) {
+    if (ctid < bsz * 8 * NT) {
       const int tok = ctid / bsz, row = ctid % bsz;
       if (tok < p.M && out_ok) {
         float v = 0.f;
@@ -426,8 +461,8 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
 constexpr int kMinRowCopy = 3072;
 constexpr int kRowPad = 0;  // shared-memory row padding (16 measured no faster)
 
-static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want) {
-  const int64_t room = kSmemBudget - x_bytes;
+static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want, int64_t budget) {
+  const int64_t room = budget - x_bytes;
   if (room <= 0) return false;
   for (int64_t P = 1; P <= 16; ++P) {
     if (K % (64 * P) != 0) continue;
@@ -450,30 +485,34 @@ static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want) {
 
 Plan plan(int64_t M, int64_t N, int64_t K) {
   Plan pl = {};
-  if (M < 1 || M > 8 || K % 64 != 0 || K <= 0 || N <= 0 || K > (1 << 20)) return pl;
+  if (M < 1 || M > 16 || K % 64 != 0 || K <= 0 || N <= 0 || K > (1 << 20)) return pl;
+  const int nt = M <= 8 ? 1 : 2;
+  // the static reduction array grows with the token groups (8 KB each)
+  const int64_t budget = kSmemBudget - (nt - 1) * 8 * 1024;
   const int64_t xb = ((M * K * 2) + 127) / 128 * 128;
   // x in shared memory with three slabs; else x in tensor memory (when its
   // layout fits) with three slabs; else x in shared memory with two; else x
   // from L2.  Tensor memory holds 8 columns (one 64-k chunk of 16
-  // activations per lane) per chunk a warp owns: K / 64 columns per warp,
-  // 256 available, and chunk ownership (every 8th chunk) must not change
-  // across K pieces.
+  // activations per lane) per chunk and token group a warp owns: NT K / 64
+  // columns per warp, 256 available, and chunk ownership (every 8th chunk)
+  // must not change across K pieces.
   auto tmem_fits = [&](const Plan& q) {
-    return K % 512 == 0 && K / 64 <= kTmemCols / 2 && (q.ks / 64) % kConsumers == 0;
+    return K % 512 == 0 && nt * K / 64 <= kTmemCols / 2 && (q.ks / 64) % kConsumers == 0;
   };
   Plan t = {};
-  if (try_plan(pl, xb, K, 3)) {
+  if (try_plan(pl, xb, K, 3, budget)) {
     pl.xmode = kXSmem;
-  } else if (try_plan(t, 0, K, 3) && tmem_fits(t)) {
+  } else if (try_plan(t, 0, K, 3, budget) && tmem_fits(t)) {
     pl = t;
     pl.xmode = kXTmem;
-  } else if (try_plan(pl, xb, K, 2)) {
+  } else if (try_plan(pl, xb, K, 2, budget)) {
     pl.xmode = kXSmem;
-  } else if (try_plan(pl, 0, K, 3)) {
+  } else if (try_plan(pl, 0, K, 3, budget)) {
     pl.xmode = kXL2;
   } else {
     return Plan{};
   }
+  pl.nt = nt;
   pl.smem = pl.x_bytes + pl.stages * pl.slab_bytes;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -482,16 +521,17 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   return pl;
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT, int XM>
+template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT>
 int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
-  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM>;
+  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM, NT>;
   static int configured_smem[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
+  constexpr int kMaxDyn = kSmemBudget - (NT - 1) * 8 * 1024;  // beside the static reduction array
   if (configured_smem[dev & 63] < pl.smem) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDyn) != cudaSuccess)
       return CEK_ERR_LAUNCH;
-    configured_smem[dev & 63] = kSmemBudget;
+    configured_smem[dev & 63] = kMaxDyn;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pl.grid);
@@ -506,13 +546,18 @@ int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, p, pl) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
 }
 
+template <typename InT, int F, int S, typename OutT, int NT>
+int launch_x(const GemvParams& p, const Plan& pl, cudaStream_t st) {
+  return pl.xmode == kXSmem   ? launch<InT, F, S, OutT, kXSmem, NT>(p, pl, st)
+         : pl.xmode == kXTmem ? launch<InT, F, S, OutT, kXTmem, NT>(p, pl, st)
+                              : launch<InT, F, S, OutT, kXL2, NT>(p, pl, st);
+}
+
 template <typename InT, typename OutT>
 int dispatch(const GemvParams& p, const Plan& pl, int w_fmt, int scale_kind, cudaStream_t st) {
 #define CEK_CASE(F, S) \
   if (w_fmt == F && scale_kind == S)                                    \
-    return pl.xmode == kXSmem  ? launch<InT, F, S, OutT, kXSmem>(p, pl, st)            \
-           : pl.xmode == kXTmem ? launch<InT, F, S, OutT, kXTmem>(p, pl, st)           \
-                                : launch<InT, F, S, OutT, kXL2>(p, pl, st);
+    return pl.nt == 1 ? launch_x<InT, F, S, OutT, 1>(p, pl, st) : launch_x<InT, F, S, OutT, 2>(p, pl, st);
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERN_F16)
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERN_F32)
   CEK_CASE(CEK_E4M3, CEK_SCALE_PERT_F32)
@@ -537,11 +582,12 @@ int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, i
   if (disabled) return CEK_ERR_UNSUPPORTED;
   const bulk::Plan pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K);
   if (pl.stages == 0 || (p.y_gelu && (p.nmat || p.ar_world))) return CEK_ERR_UNSUPPORTED;
-  if (x_dtype == CEK_F16 && y_dtype == CEK_F16) return bulk::dispatch<__half, __half>(p, pl, w_fmt, scale_kind, st);
-  if (x_dtype == CEK_F16 && y_dtype == CEK_BF16)
-    return bulk::dispatch<__half, __nv_bfloat16>(p, pl, w_fmt, scale_kind, st);
-  if (x_dtype == CEK_BF16 && y_dtype == CEK_F16)
-    return bulk::dispatch<__nv_bfloat16, __half>(p, pl, w_fmt, scale_kind, st);
+  // two token groups with x from L2 measured slower than the split-K kernel
+  // (down 4096 x 14336 at M = 16: 24.3 against 22.5 us)
+  if (pl.nt == 2 && pl.xmode == bulk::kXL2 && !p.y_gelu) return CEK_ERR_UNSUPPORTED;
+  // mixed activation / output types stay on the split-K kernel
+  if (x_dtype != y_dtype) return CEK_ERR_UNSUPPORTED;
+  if (x_dtype == CEK_F16) return bulk::dispatch<__half, __half>(p, pl, w_fmt, scale_kind, st);
   return bulk::dispatch<__nv_bfloat16, __nv_bfloat16>(p, pl, w_fmt, scale_kind, st);
 }
 

@@ -179,7 +179,7 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
   if (!norm_weight || !w || !scale || !workspace || (N > 0 && !y)) return CEK_ERR_INVALID_ARG;
   const bool gelu_out = (flags & CEK_GEMV_GELU_MUL_OUTPUT) != 0;
   // the gated output is formed by the bulk GEMV, which reads staged rows
-  if (gelu_out && (workspace_bytes < normed_bytes(M, K) || M > 8 || K % 64 != 0)) return CEK_ERR_UNSUPPORTED;
+  if (gelu_out && (workspace_bytes < normed_bytes(M, K) || M > 16 || K % 64 != 0)) return CEK_ERR_UNSUPPORTED;
   if (workspace_bytes < inv_rms_bytes(M)) return CEK_ERR_INVALID_ARG;
   if (!cek_host::aligned16(norm_weight) || !cek_host::aligned16(w) || !cek_host::aligned16(workspace))
     return CEK_ERR_ALIGNMENT;

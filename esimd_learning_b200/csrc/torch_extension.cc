@@ -257,7 +257,7 @@ at::Tensor esimd_fused_add_rms_norm_gelu_mul_fp8(at::Tensor hidden_states, at::T
   c10::cuda::CUDAGuard guard(hidden_states.device());
   const int64_t ws_bytes = cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, K);
   at::Tensor ws = at::empty({ws_bytes}, hidden_states.options().dtype(at::kByte));
-  const bool fused = M <= 8 && K % 64 == 0;  // what the gated bulk GEMV takes
+  const bool fused = M <= 16 && K % 64 == 0;  // what the gated bulk GEMV takes
   at::Tensor gu = fused ? output : at::empty({M, 2 * N}, output.options());
   check_status(cek_fused_add_rmsnorm_gemv_fp8(hidden_states.data_ptr(), residual.data_ptr(), weight.data_ptr(),
                                               (float)eps, qweight.data_ptr(), qweight_scale.data_ptr(), gu.data_ptr(),

@@ -10,12 +10,12 @@ e5m2) with an fp32 ``weight_scale``, per output channel [N] or per tensor
 ops' arithmetic (no activation quantisation):
 
 * M <= 64 tokens: the GEMV family (``esimd_gemv_fp8_pern``, the bulk-copy
-  kernel for M <= 8): one weight pass per 16-token tile;
-* M > 64 (prefill): ``cek_gemm_fp8w``.  The weight is first dequantised
-  exactly into a 16-bit workspace taken from the caching allocator for the
-  call, then a ``kind::f16`` tcgen05 GEMM runs with the scale in its
-  epilogue.  K % 64 == 0 and N % 16 == 0 are needed; other shapes stay on the
-  GEMV family.
+  kernel for M <= 16): one weight pass per 16-token tile;
+* M > 64 (prefill): ``cek_gemm_fp8w``, a ``kind::f16`` tcgen05 GEMM on the
+  weight converted exactly to 16 bits (in shared memory up to 256 tokens,
+  into a workspace taken from the caching allocator for the call above), the
+  scale in its epilogue.  K % 64 == 0 and N % 16 == 0 are needed; other
+  shapes stay on the GEMV family.
 
 ``layer`` is any ``torch.nn.Module``; nothing here imports vLLM.
 """

@@ -79,8 +79,8 @@ CEK_API const char* cek_version(void);
  *   y[m, n] = io( gelu_tanh(f32 g) * f32 u ),  g = io(GEMV row n),
  *   u = io(GEMV row N + n),
  * i.e. bit for bit the plain GEMV into [M, 2N] followed by cek_gelu_and_mul,
- * in one launch and without the [M, 2N] round trip.  Supported for M <= 8
- * and K % 64 == 0; otherwise CEK_ERR_UNSUPPORTED and nothing runs.  New: the
+ * in one launch and without the [M, 2N] round trip.  Supported for M <= 16,
+ * K % 64 == 0 and x_dtype == y_dtype; otherwise CEK_ERR_UNSUPPORTED and nothing runs.  New: the
  * reference has no GeLU op. */
 #define CEK_GEMV_GELU_MUL_OUTPUT 2u
 CEK_API int cek_gemv_fp8(const void* x, const void* w, const void* scale, void* y,
@@ -124,7 +124,7 @@ CEK_API int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* weig
  * flags: CEK_GEMV_EARLY_WEIGHTS is accepted and implied (the weight stream
  * always starts early here: the stats kernel never writes w);
  * CEK_GEMV_GELU_MUL_OUTPUT makes the projection the gated gate_up one of
- * cek_gemv_fp8 (w [2N, K], y [M, N]); it needs the full workspace, M <= 8 and
+ * cek_gemv_fp8 (w [2N, K], y [M, N]); it needs the full workspace, M <= 16 and
  * K % 64 == 0, else CEK_ERR_UNSUPPORTED before anything runs.
  * M <= 16, K % 8 == 0, K <= 16384.  No reference counterpart: the reference
  * runs fused_add_rms_norm_batched_host and GEMV_fp8_pern_host as two ops. */
@@ -253,7 +253,7 @@ CEK_API int cek_gemm_fp8w(const void* x, const void* w, const void* scale, void*
                           int64_t K, int dtype, int w_fmt, int scale_kind, void* stream);
 
 /* Number of bounded device waits in the bulk-copy GEMV kernel (the
- * cek_gemv_fp8 path for up to 8 tokens) that gave up since the library was
+ * cek_gemv_fp8 path for up to 16 tokens) that gave up since the library was
  * loaded (0 in a healthy run).  Synchronous. */
 CEK_API int cek_gemv_fp8_timeouts(uint64_t* count);
 

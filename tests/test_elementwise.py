@@ -76,14 +76,16 @@ def _gated_case(M, N, K, io, seed):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 512, 1024), (3, 1000, 4096), (8, 256, 2048), (1, 3584, 8192),
-                                   (2, 1500, 14336), (8, 4096, 8192), (5, 9, 64), (12, 256, 1024)])
+                                   (2, 1500, 14336), (8, 4096, 8192), (5, 9, 64), (12, 256, 1024),
+                                   (16, 1000, 4096), (20, 256, 1024)])
 @pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
 def test_gemv_gelu_mul(ext, cuda_device, M, N, K, io):
     """The gated GEMV equals the plain GEMV into [M, 2N] followed by
     esimd_gelu_and_mul, bit for bit (same GEMV sums, same rounding of gate
-    and up, same pinned GeLU arithmetic), for the fused kernel (M <= 8,
-    ragged N, K cut into pieces, x read from L2 at M = 8, K = 8192) and for
-    the op's two-launch fallback (M = 12).  Both agree with the oracle."""
+    and up, same pinned GeLU arithmetic), for the fused kernel (M <= 16,
+    ragged N, K cut into pieces, x in tensor memory at M = 8, K = 8192, two
+    token groups at M = 12, 16) and for the op's two-launch fallback
+    (M = 20).  Both agree with the oracle."""
     import esimd_learning_b200 as ops
 
     x, wq, sc = _gated_case(M, N, K, io, seed=M * 1000 + N)
@@ -103,7 +105,7 @@ def test_gemv_gelu_mul(ext, cuda_device, M, N, K, io):
 def test_fused_norm_gelu_mul(ext, cuda_device, M):
     """add + RMSNorm + gated gate_up GEMV + GeLU-and-mul equals the fused-norm
     op into [M, 2N] followed by esimd_gelu_and_mul, bit for bit, including the
-    residual update (M = 16 takes the two-launch fallback)."""
+    residual update (M = 16: two token groups)."""
     import esimd_learning_b200 as ops
     from esimd_learning_b200.workloads import make_fp8_weight
 
@@ -133,7 +135,7 @@ def test_fused_norm_gelu_mul(ext, cuda_device, M):
 def test_gelu_mul_output_flag_cabi(cuda_device):
     """C ABI: CEK_GEMV_GELU_MUL_OUTPUT (N = output columns, w has 2N rows)
     runs where the gated kernel fits and returns CEK_ERR_UNSUPPORTED,
-    launching nothing, where it does not (M > 8, K % 64 != 0)."""
+    launching nothing, where it does not (M > 16, K % 64 != 0)."""
     x, wq, sc = _gated_case(2, 300, 4096, torch.float16, seed=5)
     xd, wd, sd = x.to(cuda_device), wq.to(cuda_device), sc.to(cuda_device)
     y = torch.zeros(2, 300, dtype=torch.float16, device=cuda_device)
@@ -143,7 +145,7 @@ def test_gelu_mul_output_flag_cabi(cuda_device):
     torch.cuda.synchronize()
     O.assert_parity(y, O.gelu_and_mul(O.gemv_fp8(x, wq, sc)), "flag")
     L = cabi.lib()
-    for M, K in ((12, 4096), (2, 4080)):
+    for M, K in ((17, 4096), (2, 4080)):
         xb = torch.zeros(M, K, dtype=torch.float16, device=cuda_device)
         yb = torch.zeros(M, 300, dtype=torch.float16, device=cuda_device)
         rc = L.cek_gemv_fp8(cabi.ptr(xb), cabi.ptr(wd), cabi.ptr(sd), cabi.ptr(yb), M, 300, K, cabi.CEK_F16,

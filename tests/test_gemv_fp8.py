@@ -162,12 +162,16 @@ def test_ragged_shapes(cuda_device, M, N, K, io, flags):
 @pytest.mark.parametrize("flags", FLAGS)
 @pytest.mark.parametrize("M,N,K", [(1, 17, 64), (3, 200, 1024), (8, 1001, 512), (7, 33, 2048),
                                    (2, 2371, 14336), (1, 150, 7168), (5, 4096, 4096), (1, 1, 128),
-                                   (6, 148 * 16 + 5, 3072), (8, 777, 14336), (4, 4096, 14336)])
+                                   (6, 148 * 16 + 5, 3072), (8, 777, 14336), (4, 4096, 14336),
+                                   (9, 1000, 4096), (12, 333, 2048), (16, 4096, 14336), (16, 2049, 8192),
+                                   (11, 57, 28672)])
 @pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
 def test_bulk_path_shapes(cuda_device, M, N, K, io, flags):
-    """Shapes the bulk-copy GEMV takes (M <= 8, K % 64 == 0): ragged row
+    """Shapes the bulk-copy GEMV takes (M <= 16, K % 64 == 0): ragged row
     ranges per CTA, partial 16-row blocks, K cut into row pieces (K = 7168,
-    14336), grids smaller than the SM count.  No bounded wait may give up."""
+    14336, 28672), grids smaller than the SM count, one and two token groups,
+    x in shared memory, tensor memory and L2.  No bounded wait may give
+    up."""
     import ctypes
     x, wq, s = gemv_case(M, N, K, seed=M * 7919 + N, dtype=io)
     y = torch.full((M, N), float("nan"), dtype=io, device=cuda_device)

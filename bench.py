@@ -412,7 +412,7 @@ def vllm_compare() -> dict:
     return res
 
 
-def measure_chain(dev, rank: int, world: int, Ms=(1, 8), reps: int = 200) -> dict:
+def measure_chain(dev, rank: int, world: int, Ms=(1, 8, 16), reps: int = 200) -> dict:
     """the 70B-shaped decode step (esimd_learning_b200.chain)
     tensor-parallel over the `world` ranks of this run.  At TP > 1 the down
     projection's all-reduce runs two ways: fused into the GEMV over NVLink

@@ -165,11 +165,12 @@ gemv_fp8_kernel(const GemvParams pin) {
   c.w0 = p.w + (size_t)(c.v0 ? row0 : 0) * p.K + c.t * 16;
   c.w1 = p.w + (size_t)(c.v1 ? row1 : 0) * p.K + c.t * 16;
 
-  // Every CTA of this grid is resident once each has passed this point: let
-  // the next kernel on the stream launch into the slots the tail frees.  It
-  // waits (griddepcontrol.wait) for this grid's completion before reading
-  // anything this grid writes.
-  pdl_launch_dependents();
+  // No early griddepcontrol.launch_dependents here: the kernel that follows
+  // is often the persistent bulk GEMV (one 220 KB CTA per SM), whose CTAs,
+  // launched early, would take whole SMs from this grid's last wave while
+  // they wait (measured: the chain's down projection at M = 16 ran 80 us
+  // alone and far longer in the graph).  The dependent grid launches when
+  // this one completes.
 
   float acc[NT][4];
 #pragma unroll
@@ -276,7 +277,10 @@ static int launch_one(const GemvParams& p, const GemvLaunch& L, cudaStream_t st)
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
+  // Programmatic launch only behind the fused op's stats kernel (a few CTAs).
+  // Behind the persistent bulk GEMV it measured slower: the chain at M = 16
+  // (down projection here) took 311 us per layer with it, 209 us without.
+  attr[0].val.programmaticStreamSerializationAllowed = (cek_host::pdl_enabled() && FUSED) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_fp8_kernel<InT, FMT, SCALE, OutT, NT, FUSED>, p);

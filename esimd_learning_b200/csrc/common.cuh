@@ -163,6 +163,20 @@ inline bool pdl_enabled() {
   }();
   return on;
 }
+// SM count of the current device, cached per device (launch planning runs
+// on every call; the attribute query is host time on the hot path).
+inline int sm_count() {
+  static int cache[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& c = cache[dev & 63];
+  if (c == 0) {
+    int sms = 148;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    c = sms;
+  }
+  return c;
+}
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;

@@ -395,9 +395,9 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaSt
   auto kern = gemm_fp8_kernel<OutT, BN, KIND, WFMT>;
   constexpr int SMEM_BYTES = Tile<BN, KIND>::SMEM_BYTES;
   static unsigned attr_set = 0;
-  int dev = 0, sms = 148;
+  const int sms = cek_host::sm_count();
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned bit = 1u << (dev & 31);
   if (!(attr_set & bit)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
@@ -423,9 +423,7 @@ int choose_bn(int64_t M, int64_t N) {
   // i.e. the persistent grid's critical path.  A narrower tile must win by
   // more than 3 %: per FLOP it is slightly slower (measured: at M = 8192,
   // N = 14336 BN = 256 beats 224 although its cost is 2 % higher).
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = cek_host::sm_count();
   const int64_t num_m = (M + BM - 1) / BM;
   const int cands[4] = {256, 224, 192, 160};
   int bn = 256;

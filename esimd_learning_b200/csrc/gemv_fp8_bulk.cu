@@ -514,9 +514,7 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   }
   pl.nt = nt;
   pl.smem = pl.x_bytes + pl.stages * pl.slab_bytes;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = cek_host::sm_count();
   pl.grid = (int)std::min<int64_t>(sms, (N + kSlabRows - 1) / kSlabRows);
   return pl;
 }

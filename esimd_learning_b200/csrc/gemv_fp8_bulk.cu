@@ -59,7 +59,7 @@ constexpr int kAcc = 2;  // independent accumulators (shorter MMA dependency cha
 constexpr int kThreads = 32 * (1 + kConsumers);
 constexpr int kSlabRows = 16;  // a row block: the m16 A operand of the MMA
 constexpr int kMaxStages = 8;
-constexpr uint32_t kPiece = 8192;          // bytes per bulk copy of a contiguous slab
+constexpr uint32_t kPiece = 8192;  // bytes per bulk copy of a contiguous slab (16 / 32 KB: no faster)
 constexpr int kSmemBudget = 216 * 1024;    // dynamic shared memory per CTA (static: ~8.3 KB)
 constexpr uint32_t kWaitPolls = 1u << 22;
 constexpr int kXBatch = 8;                 // chunks per batch when x is read from global memory

@@ -13,7 +13,10 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from esimd_learning_b200.chain import SMALL, DecodeChain, full_weights, shard_weights
+from esimd_learning_b200.chain import SMALL, ChainShape, DecodeChain, full_weights, shard_weights
+
+# a small layer with 4 kv heads, so that TP = 4 shards them
+SMALL4 = ChainShape(hidden=1024, num_q_heads=8, num_kv_heads=4, head_dim=128, intermediate=2048, max_position=512)
 from oracle import oracle as O
 
 
@@ -34,11 +37,11 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, shape):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    shape, M = SMALL, 3
+    M = 3
     full = full_weights(shape, seed=0)
     sh = shard_weights(full, shape, rank, world)
     h, r, a, pos = _inputs(shape, M)
@@ -55,12 +58,12 @@ def _rank_main(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_tp2_sharding_matches_unsharded_oracle():
-    world = 2
+@pytest.mark.parametrize("world,shape", [(2, SMALL), (4, SMALL4)], ids=["tp2", "tp4"])
+def test_tp_sharding_matches_unsharded_oracle(world, shape):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, shape)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -70,7 +73,6 @@ def test_tp2_sharding_matches_unsharded_oracle():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    shape = SMALL
     full = full_weights(shape, seed=0)
     h, r, a, pos = _inputs(shape, 3)
     out, qkv, r2 = O.decode_chain(full, shape, h, r, a, pos)

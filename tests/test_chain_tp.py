@@ -54,7 +54,9 @@ def _rank_main(rank, world, port, q, shape):
     act = O.gelu_and_mul(gu)
     part = O.gemv_fp8(act, *sh["down"], out_dtype=torch.float32)
     dist.all_reduce(part)
-    q.put((rank, part.half(), qkv, r2))
+    # plain numpy copies: torch tensors in a queue are shared through the
+    # sender's file descriptors, which break if this process exits first
+    q.put((rank, part.half().numpy().copy(), qkv.numpy().copy(), r2.numpy().copy()))
     dist.destroy_process_group()
 
 
@@ -69,7 +71,7 @@ def test_tp_sharding_matches_unsharded_oracle(world, shape):
     res = {}
     for _ in range(world):
         rank, out, qkv, r2 = q.get(timeout=300)
-        res[rank] = (out, qkv, r2)
+        res[rank] = tuple(torch.from_numpy(a) for a in (out, qkv, r2))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

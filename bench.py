@@ -165,8 +165,33 @@ def max_over_ranks(v: float, world: int) -> float:
 
 # ---- our arm ------------------------------------------------------------------------
 
+def workloads():
+    """esimd_learning_b200/workloads.py loaded by path: the seeded input
+    builders only, without the package __init__ (which loads the CUDA
+    extensions), so the CPU reference arm maps none of this build's .so files."""
+    import importlib.util
+    mod = sys.modules.get("cek_bench_workloads")
+    if mod is None:
+        spec = importlib.util.spec_from_file_location("cek_bench_workloads",
+                                                      ROOT / "esimd_learning_b200" / "workloads.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        sys.modules["cek_bench_workloads"] = mod
+    return mod
+
+
+def arm_config(world: int, prefetch: bool) -> dict:
+    """The `config` object of the JSON line; both arms print exactly this."""
+    return {"workload": "BASELINE config 1: batched FP8 GEMV, per-channel fp32 scales",
+            "shapes": {n: [N, K] for n, N, K in SHAPES}, "M": MS,
+            "l2": "2 weight sets alternating with M: > 126 MB (L2) between two reads of one weight",
+            "timing": "CUDA graph of the 12 launches per step, CUDA events",
+            "weight_prefetch": prefetch,
+            "parallelism": f"replicas x{world} (independent GEMV sweeps)"}
+
+
 def build_sets(dev, n_sets: int = 2):
-    from esimd_learning_b200.workloads import make_fp8_weight
+    make_fp8_weight = workloads().make_fp8_weight
 
     gen = torch.Generator().manual_seed(0)
     sets = []
@@ -312,12 +337,7 @@ def run_ours(args, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "e4m3*fp16->fp32", "data": "synthetic (seed 0: x~N(0,1) fp16, W~N(0,0.02) per-row e4m3)",
-        "config": {"workload": "BASELINE config 1: batched FP8 GEMV, per-channel fp32 scales",
-                   "shapes": {n: [N, K] for n, N, K in SHAPES}, "M": MS,
-                   "l2": "2 weight sets alternating with M: > 126 MB (L2) between two reads of one weight",
-                   "timing": "CUDA graph of the 12 launches per step, CUDA events",
-                   "weight_prefetch": prefetch,
-                   "parallelism": f"replicas x{world} (independent GEMV sweeps)"},
+        "config": arm_config(world, prefetch),
         "us_per_call": {k: round(v, 3) for k, v in per_call.items()},
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
@@ -586,7 +606,7 @@ def measure_gemm(dev, M: int, reps: int = 20) -> dict:
 
 def _cpu_setup():
     torch.set_num_threads(os.cpu_count() or 1)
-    from esimd_learning_b200.workloads import make_fp8_weight
+    make_fp8_weight = workloads().make_fp8_weight
     gen = torch.Generator().manual_seed(0)
     ws = {name: make_fp8_weight(N, K, gen) for name, N, K in SHAPES}
     xs = {(name, M): torch.randn(M, K, generator=gen).to(torch.float16)
@@ -665,9 +685,9 @@ def run_reference(args, rank, world):
             "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3*fp16->fp32",
             "data": "synthetic (seed 0)", "impl": "reference",
-            "config": {"workload": "BASELINE config 1: batched FP8 GEMV, per-channel fp32 scales",
-                       "reference_path": "oracle port of the reference tests' torch CPU oracle "
-                                         "(the reference kernels are Intel-XPU ESIMD only)"},
+            "config": arm_config(world, not args.no_prefetch),
+            "reference_path": "oracle port of the reference tests' torch CPU oracle "
+                              "(the reference kernels are Intel-XPU ESIMD only)",
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores,
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,

@@ -1,29 +1,24 @@
-"""B200 (sm_100a) FP8 custom-op package: a drop-in for the reference's
-`custom_esimd_kernels_vllm` Python package
-(python/custom_esimd_kernels_vllm/__init__.py:1-13).
+"""B200 (sm_100a) implementation of the FP8 custom-op path.
 
-Importing it loads the two torch.library extension modules, which register
-the ops in the `torch.ops.custom_esimd_kernels_vllm` namespace on the CUDA
-dispatch key, and re-exports the Python wrappers of `ops`.  A vLLM build that
-calls `torch.ops.custom_esimd_kernels_vllm.*` or `from custom_esimd_kernels_vllm
-import ...` can point at this package instead (`import esimd_learning_b200 as
-custom_esimd_kernels_vllm`).
-
-There is no CPU or eager fallback: if the extensions were not built the import
-fails with the command that builds them.
+The kernels are in `libcek_b200.so` (C ABI: include/cek.h); the torch.library
+registration and the Python wrappers are the package `custom_esimd_kernels_vllm`
+(under `python/`, the reference's name and layout).  Importing this package
+puts `python/` on the import path, loads that wrapper package and re-exports
+its ops, so `import esimd_learning_b200 as ops; ops.esimd_gemv_fp8_pern(...)`
+and `from custom_esimd_kernels_vllm import esimd_gemv_fp8_pern` reach the same
+op.  The decode-chain driver (`chain`), the C-ABI loader (`cabi`) and the
+vLLM linear method (`vllm_linear`) live here.
 """
-import torch  # noqa: F401  (loads libtorch before the extension modules)
+import sys
+from pathlib import Path
 
-try:
-    from esimd_learning_b200 import custom_esimd_kernels  # noqa: F401
-    from esimd_learning_b200 import custom_esimd_kernels_gemm  # noqa: F401
-except ImportError as e:  # pragma: no cover - exercised only on an unbuilt tree
-    raise ImportError(
-        "esimd_learning_b200 extensions are not built; run "
-        "`python esimd_learning_b200/build.py` (needs nvcc with sm_100a support)"
-    ) from e
+_PY = str(Path(__file__).resolve().parent.parent / "python")
+if _PY not in sys.path:
+    sys.path.insert(0, _PY)
 
-from esimd_learning_b200.ops import (  # noqa: E402,F401
+import custom_esimd_kernels_vllm  # noqa: E402,F401
+from custom_esimd_kernels_vllm import ops  # noqa: E402,F401
+from custom_esimd_kernels_vllm.ops import (  # noqa: E402,F401
     esimd_gemv_fp8_pern,
     esimd_gemv_fp8_pert,
     esimd_gemv_fp8_pern_fused,

@@ -1,15 +1,19 @@
 """Build the sm_100a libraries in-tree.
 
-Outputs (next to this file):
-  libcek_b200.so                 the C-ABI kernel library (include/cek.h), nvcc
-  custom_esimd_kernels.so        torch.library registration of the GEMV /
-                                 add+RMSNorm / decode-helper ops (g++)
-  custom_esimd_kernels_gemm.so   torch.library registration of the GEMM ops
+Outputs:
+  esimd_learning_b200/libcek_b200.so
+      the C-ABI kernel library (include/cek.h), nvcc
+  python/custom_esimd_kernels_vllm/custom_esimd_kernels.so
+      torch.library registration of the GEMV / add+RMSNorm / decode-helper ops (g++)
+  python/custom_esimd_kernels_vllm/custom_esimd_kernels_gemm.so
+      torch.library registration of the GEMM ops
 
 The two extension modules keep the reference's module names and PyInit
-symbols (csrc/xpu/torch_extension.cc:21-24, torch_extension_gemm.cc:16-20) so
-`from <package> import custom_esimd_kernels, custom_esimd_kernels_gemm`
-works as in the reference's python/custom_esimd_kernels_vllm/__init__.py:3-4.
+symbols (csrc/xpu/torch_extension.cc:21-24, torch_extension_gemm.cc:16-20) and
+sit in the reference's wrapper package, so
+`from custom_esimd_kernels_vllm import custom_esimd_kernels, custom_esimd_kernels_gemm`
+works as in python/custom_esimd_kernels_vllm/__init__.py:3-4.  They find
+libcek_b200.so through a relative rpath.
 
 Run: python esimd_learning_b200/build.py [--force]
 """
@@ -26,6 +30,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 BUILD = PKG / "_build"
+WRAPPER = PKG.parent / "python" / "custom_esimd_kernels_vllm"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -97,11 +102,11 @@ def build_ext(force: bool = False) -> list[Path]:
     jobs = []
     for mod, src in EXT_MODULES.items():
         s = CSRC / src
-        out = PKG / f"{mod}.so"
+        out = WRAPPER / f"{mod}.so"
         outs.append(out)
         if force or _stale(out, [s, lib] + _headers()):
             jobs.append(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", *cflags, str(s), "-o", str(out),
-                         f"-L{PKG}", "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN", *ldflags])
+                         f"-L{PKG}", "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN/../../esimd_learning_b200", *ldflags])
     with cf.ThreadPoolExecutor(max_workers=2) as ex:
         list(ex.map(_run, jobs))
     return outs

@@ -5,8 +5,9 @@ from pathlib import Path
 import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
-if str(ROOT) not in sys.path:
-    sys.path.insert(0, str(ROOT))
+for _p in (str(ROOT / "python"), str(ROOT)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
 
 GOLDEN = Path(__file__).resolve().parent / "golden" / "reference_vectors.pt"
 

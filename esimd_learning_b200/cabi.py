@@ -50,6 +50,7 @@ SIGNATURES = {
     "cek_ipc_open_handle": (_I, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "cek_ipc_close_handle": (_I, [_P]),
     "cek_comm_errors": (_I, [_P, ctypes.POINTER(ctypes.c_uint32)]),
+    "cek_comm_reset": (_I, [_P, _I64]),
     "cek_gemv_fp8_allreduce": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _I64, _I, _I, _U, _P]),
     "cek_gemm_fp8_scaled": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "cek_gemm_fp8w_workspace_bytes": (_I64, [_I64, _I64]),

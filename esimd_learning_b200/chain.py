@@ -136,6 +136,7 @@ class TPComm:
         from esimd_learning_b200 import cabi
 
         self.cabi, self.rank, self.world, self.slot_elems = cabi, rank, world, slot_elems
+        self.group = group
         L = cabi.lib()
         nbytes = L.cek_tp_comm_bytes(slot_elems, world)
         if nbytes <= 0:
@@ -165,6 +166,14 @@ class TPComm:
         v = ctypes.c_uint32(0)
         self.cabi.call("cek_comm_errors", self.mine, ctypes.byref(v))
         return v.value
+
+    def reset(self):
+        """Recovery after a reported timeout: every rank calls this with no
+        call in flight on any rank (the group barriers on both sides)."""
+        import torch.distributed as dist
+        dist.barrier(group=self.group)
+        self.cabi.call("cek_comm_reset", self.mine, self.cabi.lib().cek_tp_comm_bytes(self.slot_elems, self.world))
+        dist.barrier(group=self.group)
 
     def close(self):
         for p in self.opened:

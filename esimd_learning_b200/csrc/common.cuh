@@ -7,6 +7,7 @@
 // computes (tests/test_gemv_fp8.py:31-32); both FP8 formats embed exactly in
 // fp16 and in bf16, so no rounding happens on the weight path.
 #pragma once
+#include <atomic>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -163,19 +164,40 @@ inline bool pdl_enabled() {
   }();
   return on;
 }
+// Per-device host caches (SM count, configured shared-memory size).  Slots
+// are atomics, so host threads launching concurrently see either the old or
+// the new value; both writers store the same value, and the cached work
+// (an attribute query, cudaFuncSetAttribute) is idempotent.  Ordinals at or
+// above kMaxCachedDevices are not cached: the work is redone on every call.
+constexpr int kMaxCachedDevices = 64;
+struct DeviceSlots {
+  std::atomic<int> v[kMaxCachedDevices] = {};
+  std::atomic<int>* at(int dev) { return dev >= 0 && dev < kMaxCachedDevices ? &v[dev] : nullptr; }
+};
 // SM count of the current device, cached per device (launch planning runs
 // on every call; the attribute query is host time on the hot path).
 inline int sm_count() {
-  static int cache[64] = {};
+  static DeviceSlots cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  int& c = cache[dev & 63];
-  if (c == 0) {
-    int sms = 148;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-    c = sms;
+  std::atomic<int>* c = cache.at(dev);
+  int v = c ? c->load(std::memory_order_relaxed) : 0;
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    if (c) c->store(v, std::memory_order_relaxed);
   }
-  return c;
+  return v;
+}
+// Raise a kernel's dynamic shared-memory limit to `bytes` once per device.
+template <typename Kern>
+inline bool ensure_smem_attr(DeviceSlots& slots, Kern kern, int bytes) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>* c = slots.at(dev);
+  if (c && c->load(std::memory_order_relaxed) >= bytes) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  if (c) c->store(bytes, std::memory_order_relaxed);
+  return true;
 }
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

@@ -394,16 +394,9 @@ template <typename OutT, int BN, int KIND, int WFMT = 0>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t st) {
   auto kern = gemm_fp8_kernel<OutT, BN, KIND, WFMT>;
   constexpr int SMEM_BYTES = Tile<BN, KIND>::SMEM_BYTES;
-  static unsigned attr_set = 0;
+  static cek_host::DeviceSlots attr_set;
   const int sms = cek_host::sm_count();
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const unsigned bit = 1u << (dev & 31);
-  if (!(attr_set & bit)) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
-      return CEK_ERR_LAUNCH;
-    attr_set |= bit;
-  }
+  if (!cek_host::ensure_smem_attr(attr_set, kern, SMEM_BYTES)) return CEK_ERR_LAUNCH;
   const int tiles = p.num_m * p.num_n;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(tiles < sms ? tiles : sms));

@@ -218,6 +218,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     }
     if (!p.early_weights)
       for (int i = 0; i < pre; ++i) issue(i);
+    int issued = pre;
     for (int i = pre; i < nslabs && ok; ++i) {
       // stage i % stages is free once the consumers released use (i / stages) - 1
       if (lane == 0) ok = mbar::wait(mbar::saddr(&empty[i % stages]), ((i / stages) + 1) & 1, kWaitPolls);
@@ -227,8 +228,19 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
         break;  // the consumers' waits run out too
       }
       issue(i);
+      issued = i + 1;
     }
     if (lane == 0) TRACE(tslot, 4);
+    // The CTA's shared memory must outlive every copy into it, also when a
+    // consumer gave up waiting and exits early: wait (bounded) until the
+    // last `stages` slabs issued have landed.  Slab j's phase of stage
+    // j % stages cannot be overtaken, because nothing later was issued there.
+    if (lane == 0)
+      for (int j = max(0, issued - stages); j < issued; ++j)
+        if (!mbar::wait(mbar::saddr(&full[j % stages]), (j / stages) & 1, kWaitPolls)) {
+          atomicAdd(&g_timeouts, 1ull);
+          break;
+        }
     return;
   }
 
@@ -522,15 +534,9 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
 template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT>
 int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM, NT>;
-  static int configured_smem[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
+  static cek_host::DeviceSlots configured_smem;
   constexpr int kMaxDyn = kSmemBudget - (NT - 1) * 8 * 1024;  // beside the static reduction array
-  if (configured_smem[dev & 63] < pl.smem) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDyn) != cudaSuccess)
-      return CEK_ERR_LAUNCH;
-    configured_smem[dev & 63] = kMaxDyn;
-  }
+  if (!cek_host::ensure_smem_attr(configured_smem, kern, kMaxDyn)) return CEK_ERR_LAUNCH;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pl.grid);
   cfg.blockDim = dim3(kThreads);

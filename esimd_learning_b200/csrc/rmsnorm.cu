@@ -17,6 +17,7 @@
 #include "gemv.cuh"
 
 #include <mutex>
+#include <utility>
 
 namespace cek {
 
@@ -218,28 +219,63 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
 // op's workspace for CEK_NOALLOC_MAX_ROWS rows (256 bytes).  Host code must
 // not hand `g_noalloc_inv_rms` itself to a kernel: on the host that name is a
 // shadow variable, not device memory.  It passes the device address that
-// cudaGetSymbolAddress returns for the current device, looked up on the first
-// call on each device and cached.
+// cudaGetSymbolAddress returns in the calling thread's current CUDA context.
+// That address belongs to the context it was looked up in (a module is loaded
+// once per context), so the cache holds one entry per device, tagged with the
+// unique ID of the context (cuCtxGetId, reached through the runtime's driver
+// entry-point query so the library needs no libcuda link): a call from another
+// context on the same device, or from the context the runtime re-creates after
+// cudaDeviceReset, looks the address up again.
 constexpr int kNoallocFloats =
     int((CEK_NOALLOC_MAX_ROWS * sizeof(float) + 255) / 256 * 256 / sizeof(float));
 static __device__ __align__(256) float g_noalloc_inv_rms[kNoallocFloats];
 
 namespace {
 constexpr int kMaxDevices = 64;
+struct NoallocEntry { unsigned long long ctx_id; float* addr; };
 std::mutex g_noalloc_mu;
-float* g_noalloc_addr[kMaxDevices] = {};
+NoallocEntry g_noalloc[kMaxDevices] = {};
+
+// The current context's unique ID (0 when it cannot be read: the cache is then
+// bypassed and the address looked up on every call).
+unsigned long long current_context_id() {
+  using GetCurrent = int (*)(void**);
+  using GetId = int (*)(void*, unsigned long long*);
+  static const std::pair<GetCurrent, GetId> fns = [] {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaDriverEntryPointQueryResult qa = cudaDriverEntryPointSymbolNotFound, qb = qa;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &a, 12000, cudaEnableDefault, &qa) != cudaSuccess ||
+        qa != cudaDriverEntryPointSuccess)
+      a = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &b, 12000, cudaEnableDefault, &qb) != cudaSuccess ||
+        qb != cudaDriverEntryPointSuccess)
+      b = nullptr;
+    return std::make_pair(reinterpret_cast<GetCurrent>(a), reinterpret_cast<GetId>(b));
+  }();
+  if (!fns.first || !fns.second) return 0;
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (fns.first(&ctx) != 0 || !ctx || fns.second(ctx, &id) != 0) return 0;
+  return id;
+}
 
 int noalloc_scratch(float** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CEK_ERR_LAUNCH;
   if (dev < 0 || dev >= kMaxDevices) return CEK_ERR_UNSUPPORTED;
+  // cudaGetSymbolAddress makes the runtime bind (or create) the device's
+  // context first, so the context ID is read after it on a miss
+  const unsigned long long id = current_context_id();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+  NoallocEntry& e = g_noalloc[dev];
+  if (id == 0 || e.ctx_id != id || !e.addr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_inv_rms) != cudaSuccess || !p) return CEK_ERR_LAUNCH;
-    g_noalloc_addr[dev] = static_cast<float*>(p);
+    e.addr = static_cast<float*>(p);
+    e.ctx_id = current_context_id();
   }
-  *out = g_noalloc_addr[dev];
+  *out = e.addr;
   return CEK_OK;
 }
 }  // namespace

@@ -134,6 +134,15 @@ extern "C" int cek_comm_errors(void* my_comm, uint32_t* out) {
   return CEK_OK;
 }
 
+// Zeroes the whole region (epoch, ready flags, reduce counter, error word,
+// slots) and waits for it: the recovery step after a reported timeout, run on
+// every rank with no call in flight on any rank.
+extern "C" int cek_comm_reset(void* my_comm, int64_t bytes) {
+  if (!my_comm || bytes < (int64_t)cek::tp::kSyncBytes) return CEK_ERR_INVALID_ARG;
+  if (cudaMemset(my_comm, 0, (size_t)bytes) != cudaSuccess) return CEK_ERR_LAUNCH;
+  return cudaDeviceSynchronize() == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
+}
+
 extern "C" int cek_gemv_fp8_allreduce(const void* x, const void* w, const void* scale, void* out, int64_t M,
                                       int64_t N, int64_t K, int dtype, int w_fmt, int scale_kind,
                                       const uint64_t* peer_comm, void* my_comm, int64_t slot_elems, int rank,

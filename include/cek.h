@@ -144,15 +144,24 @@ CEK_API int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual,
  * handed out by its own pool at start-up, or a serving loop that must not
  * touch an allocator per request.  They pass inputs and outputs only.
  *
- * Computes exactly what cek_fused_add_rmsnorm_gemv_fp8 computes.  Its per-row
- * inverse-RMS scratch is a fixed device array inside libcek_b200.so, sized
- * for CEK_NOALLOC_MAX_ROWS rows (256 bytes); every GPU that loads the
- * library holds it until the process exits.  M > CEK_NOALLOC_MAX_ROWS returns
- * CEK_ERR_SCRATCH_LIMIT.  The array needs no clearing (each call writes every
- * row it later reads), but all calls share it: calls that overlap on the GPU
- * (different streams, or different host threads on one device) race.
- * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress with that device current); make that first call
+ * Computes what cek_fused_add_rmsnorm_gemv_fp8 computes when that entry point
+ * is given only the small inverse-RMS workspace: the same residual bits, and
+ * a projection within the GEMV tolerance of the full-workspace result (the
+ * normalised operand is formed in a different place, so it is not
+ * bit-identical).  CEK_GEMV_GELU_MUL_OUTPUT is refused with
+ * CEK_ERR_UNSUPPORTED: the gated output needs the full workspace.
+ * Its per-row inverse-RMS scratch is a fixed device array inside
+ * libcek_b200.so, sized for CEK_NOALLOC_MAX_ROWS rows (256 bytes); every GPU
+ * that loads the library holds it until the process exits.
+ * M > CEK_NOALLOC_MAX_ROWS returns CEK_ERR_SCRATCH_LIMIT.  The array needs no
+ * clearing (each call writes every row it later reads), but all calls share
+ * it: calls that overlap on the GPU (different streams, or different host
+ * threads on one device) race.
+ * The array's device address is looked up (cudaGetSymbolAddress) by the first
+ * call in each CUDA context, with that context current, and cached per device
+ * under the context's unique ID; a call from a different context on the same
+ * device (a non-primary context, or the one re-created after
+ * cudaDeviceReset) looks it up again.  Make the first call in a context
  * before any stream capture.  No counterpart in the reference. */
 #define CEK_NOALLOC_MAX_ROWS 16
 CEK_API int cek_fused_add_rmsnorm_gemv_fp8_noalloc(const void* hidden, void* residual,
@@ -203,7 +212,12 @@ CEK_API int cek_quant_fp8_per_token(const void* a, void* aq, float* a_scale, int
  * the slots in rank order and writes `out`.
  * M * N <= slot_elems; K % 16 == 0; one call at a time per region.
  * Bounded waits that run out set bit 0 of the region's error word
- * (cek_comm_errors).  No reference counterpart: the reference is single-GPU.
+ * (cek_comm_errors).  The word is sticky: after a timeout the ranks' epochs
+ * may disagree, so the call's output and every later one are suspect until
+ * the regions are reset.  Recovery: stop launching on every rank, agree on the
+ * host (a store or a barrier), then cek_comm_reset every rank's region (zeroes
+ * epoch, flags, error word and slots; synchronising) before the next call.
+ * No reference counterpart: the reference is single-GPU.
  * cek_comm_alloc / cek_comm_free / the IPC calls are set-up calls (they
  * allocate or map memory and synchronise); the GEMV call does neither. */
 #define CEK_IPC_HANDLE_BYTES 64
@@ -214,6 +228,7 @@ CEK_API int cek_ipc_get_handle(void* ptr, void* handle);
 CEK_API int cek_ipc_open_handle(const void* handle, void** ptr);
 CEK_API int cek_ipc_close_handle(void* ptr);
 CEK_API int cek_comm_errors(void* my_comm, uint32_t* out);
+CEK_API int cek_comm_reset(void* my_comm, int64_t bytes);
 CEK_API int cek_gemv_fp8_allreduce(const void* x, const void* w, const void* scale, void* out,
                                    int64_t M, int64_t N, int64_t K, int dtype, int w_fmt,
                                    int scale_kind, const uint64_t* peer_comm, void* my_comm,

@@ -45,6 +45,10 @@ def test_allreduce_wait_times_out_and_reports(cuda_device):
         err = ctypes.c_uint32(0)
         cabi.call("cek_comm_errors", regions[0], ctypes.byref(err))
         assert err.value & 1, "the missing rank was not reported"
+        # recovery: the reset clears the sticky error word
+        cabi.call("cek_comm_reset", regions[0], nbytes)
+        cabi.call("cek_comm_errors", regions[0], ctypes.byref(err))
+        assert err.value == 0
         # the context is still healthy
         y = torch.zeros(M, N, dtype=torch.float16, device=cuda_device)
         cabi.call("cek_gemv_fp8", cabi.ptr(x), cabi.ptr(wq), cabi.ptr(s), cabi.ptr(y), M, N, K, cabi.CEK_F16,

@@ -51,3 +51,14 @@ def test_noalloc_rejects_rows_above_its_scratch(cuda_device):
                                                            0, 0, None)
     assert rc == cabi.CEK_ERR_SCRATCH_LIMIT
     assert b"no-allocation" in cabi.lib().cek_status_string(rc)
+
+
+def test_noalloc_refuses_gated_output(cuda_device):
+    M, N, K = 2, 256, 512
+    h, r, g, wq, s = fused_norm_case(M, N=2 * N, K=K, seed=3, device=cuda_device)
+    y = torch.zeros(M, N, dtype=h.dtype, device=cuda_device)
+    rc = cabi.lib().cek_fused_add_rmsnorm_gemv_fp8_noalloc(
+        cabi.ptr(h), cabi.ptr(r), cabi.ptr(g), 1e-6, cabi.ptr(wq), cabi.ptr(s), cabi.ptr(y), M, N, K,
+        cabi.io_dtype(h), cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, cabi.CEK_GEMV_GELU_MUL_OUTPUT,
+        cabi.current_stream())
+    assert rc == cabi.CEK_ERR_UNSUPPORTED

@@ -116,6 +116,33 @@ def test_chain_tp1_gpu_vs_oracle(ext, cuda_device, M):
 
 
 @pytest.mark.gpu
+def test_chain_tp1_full_shape_gpu_vs_oracle(ext, cuda_device):
+    """BASELINE config 4 at its real shape (hidden 8192, QKV 10240 x 8192,
+    gate_up 57344 x 8192, down 8192 x 28672) at TP = 1 and M = 1, 8, 16: every
+    output of the step against the unsharded CPU oracle.  This reaches the
+    paths only full size takes: the down projection's K = 28672 (x read from
+    L2 by the bulk GEMV at M = 8, the split-K kernel at M = 16) and the
+    gated gate_up GEMV over 57344 rows."""
+    shape = ChainShape()
+    full = full_weights(shape, seed=11, device=cuda_device)
+    shards = shard_weights(full, shape, 0, 1)
+    full_cpu = {k: (tuple(t.cpu() for t in v) if isinstance(v, tuple) else v.cpu()) for k, v in full.items()}
+    del full
+    for M in (1, 8, 16):
+        chain = DecodeChain(shards, shape, M, cuda_device)
+        h, r, a, pos = _inputs(shape, M, seed=100 + M)
+        hd, rd, ad, pd = (t.to(cuda_device) for t in (h, r, a, pos))
+        out, qkv = chain.step(hd, rd, ad, pd)
+        torch.cuda.synchronize()
+        ref_out, ref_qkv, ref_r = O.decode_chain(full_cpu, shape, h, r, a, pos)
+        assert torch.equal(rd.cpu(), ref_r), f"M={M} residual"
+        O.assert_parity(qkv, ref_qkv, f"M={M} qkv")
+        O.assert_parity(out, ref_out, f"M={M} out")
+        del chain
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.gpu
 def test_chain_tp_nccl_gpu():
     """TP=2 on two GPUs with NCCL (skipped on a one-GPU box)."""
     import subprocess

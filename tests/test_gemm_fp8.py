@@ -156,6 +156,21 @@ def test_tcgen05_gemm_config3(ext, cuda_device, M):
     full = (a[rows].float() @ (bq.float() * bs[:, None]).T)
     m = O.parity(y.cpu()[rows], full)
     assert m["mean_rel"] < 0.05
+    # every row: the oracle's formula in plain fp32 torch on the GPU (exact
+    # FP8 -> fp32 decode from the oracle's table, true fp32 matmul, no TF32),
+    # itself pinned to the CPU oracle on the sampled rows above
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        af = O.fp8_decode(aq.cpu(), O.E4M3).reshape(M, K).to(dev)
+        bf = O.fp8_decode(bq, O.E4M3).reshape(N, K).to(dev)
+        ref_all = ((af @ bf.T) * as_.reshape(-1, 1) * bs.to(dev).reshape(1, -1)).half()
+        del af, bf
+        O.assert_parity(ref_all[rows].cpu(), ref, f"fp32 GPU reference vs CPU oracle M={M}")
+        for r0 in range(0, M, 1024):  # every row, in blocks (the metric is per block)
+            O.assert_parity(y[r0:r0 + 1024], ref_all[r0:r0 + 1024], f"config3 M={M} rows {r0}..")
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old_tf32
 
 
 def test_tcgen05_gemm_cabi_and_timeouts(cuda_device):

@@ -22,6 +22,7 @@ CEK_E4M3, CEK_E5M2 = 0, 1
 CEK_SCALE_PERN_F16, CEK_SCALE_PERN_F32, CEK_SCALE_PERT_F32 = 0, 1, 2
 CEK_GEMV_EARLY_WEIGHTS = 1
 CEK_GEMV_GELU_MUL_OUTPUT = 2
+CEK_COMM_SYNC_BYTES = 4096  # data area offset inside a comm region (include/cek.h)
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -51,6 +52,9 @@ SIGNATURES = {
     "cek_ipc_close_handle": (_I, [_P]),
     "cek_comm_errors": (_I, [_P, ctypes.POINTER(ctypes.c_uint32)]),
     "cek_comm_reset": (_I, [_P, _I64]),
+    "cek_comm_barrier": (_I, [_P, _P, _I, _I, _P]),
+    "cek_gemv_fp8_allgather": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _I, _I, _P, _P, _I64,
+                                    _I, _I, _U, _P]),
     "cek_gemv_fp8_allreduce": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _I64, _I, _I, _U, _P]),
     "cek_gemm_fp8_scaled": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "cek_gemm_fp8w_workspace_bytes": (_I64, [_I64, _I64]),

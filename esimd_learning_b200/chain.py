@@ -128,7 +128,9 @@ class TPComm:
     this process, and a device array of all regions' addresses.  Set-up only
     (allocates, maps, synchronises); the per-step call does neither."""
 
-    def __init__(self, slot_elems: int, rank: int, world: int, device, group=None):
+    def __init__(self, slot_elems: int, rank: int, world: int, device, group=None, data_bytes: int | None = None):
+        """slot_elems sizes the all-reduce receive slots; data_bytes, when
+        given, sizes the data area directly (all-gather outputs)."""
         import ctypes
 
         import torch.distributed as dist
@@ -136,18 +138,22 @@ class TPComm:
         from esimd_learning_b200 import cabi
 
         self.cabi, self.rank, self.world, self.slot_elems = cabi, rank, world, slot_elems
-        self.group = group
+        self.group, self.device = group, device
         L = cabi.lib()
-        nbytes = L.cek_tp_comm_bytes(slot_elems, world)
+        nbytes = (cabi.CEK_COMM_SYNC_BYTES + int(data_bytes) if data_bytes is not None
+                  else L.cek_tp_comm_bytes(slot_elems, world))
         if nbytes <= 0:
             raise ValueError("bad comm size")
+        self.nbytes = nbytes
         mine = ctypes.c_void_p()
         cabi.call("cek_comm_alloc", nbytes, ctypes.byref(mine))
         self.mine = mine.value
         handle = ctypes.create_string_buffer(64)
         cabi.call("cek_ipc_get_handle", self.mine, handle)
-        handles = [None] * world
-        dist.all_gather_object(handles, handle.raw, group=group)
+        handles = [handle.raw]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle.raw, group=group)
         self.opened = []
         addrs = []
         for r, h in enumerate(handles):
@@ -159,7 +165,31 @@ class TPComm:
                 self.opened.append(p.value)
                 addrs.append(p.value)
         self.peers = torch.tensor(addrs, dtype=torch.int64, device=device)
-        dist.barrier(group=group)
+        if world > 1:
+            dist.barrier(group=group)
+
+    def data_tensor(self, byte_offset: int, shape, dtype=torch.float16) -> torch.Tensor:
+        """A zero-copy tensor over this rank's data area at byte_offset."""
+        n = 1
+        for d in shape:
+            n *= d
+        esz = torch.empty((), dtype=dtype).element_size()
+        if byte_offset < 0 or self.cabi.CEK_COMM_SYNC_BYTES + byte_offset + n * esz > self.nbytes:
+            raise ValueError("view outside the comm region")
+
+        class _View:
+            __cuda_array_interface__ = {
+                "shape": (n * esz,), "typestr": "|u1", "version": 3, "strides": None,
+                "data": (self.mine + self.cabi.CEK_COMM_SYNC_BYTES + byte_offset, False)}
+
+        return torch.as_tensor(_View(), device=self.device).view(dtype).view(*shape)
+
+    def barrier(self, stream=None):
+        """cek_comm_barrier on the current stream: every rank's earlier pushes
+        into this region become visible here."""
+        cb = self.cabi
+        cb.call("cek_comm_barrier", cb.ptr(self.peers), self.mine, self.rank, self.world,
+                stream if stream is not None else cb.current_stream())
 
     def errors(self) -> int:
         import ctypes
@@ -182,6 +212,28 @@ class TPComm:
         if self.mine:
             self.cabi.lib().cek_comm_free(self.mine)
             self.mine = None
+
+
+def shard_rows(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Column-parallel split of n output rows: rank r owns [n r / W, n (r + 1) / W)."""
+    return n * rank // world, n * (rank + 1) // world
+
+
+def gemv_fp8_allgather(comm: TPComm, x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, row0: int,
+                       n_full: int, y_off: int, early_weights: bool = False) -> None:
+    """Column-parallel FP8 GEMV with its all-gather fused into the epilogue
+    (cek_gemv_fp8_allgather): this rank's rows [row0, row0 + w.shape[0]) of
+    y = x @ deq(W)^T * scale are stored into every rank's y [M, n_full] at
+    byte offset y_off of the comm data area.  Follow the step's calls with
+    comm.barrier()."""
+    cb = comm.cabi
+    M, K = x.shape
+    fmt = cb.CEK_E5M2 if w.dtype == torch.float8_e5m2 else cb.CEK_E4M3
+    sk = cb.CEK_SCALE_PERT_F32 if scale.numel() == 1 else (
+        cb.CEK_SCALE_PERN_F16 if scale.dtype == torch.float16 else cb.CEK_SCALE_PERN_F32)
+    cb.call("cek_gemv_fp8_allgather", cb.ptr(x), cb.ptr(w), cb.ptr(scale), M, w.shape[0], K, row0, n_full, y_off,
+            cb.io_dtype(x), fmt, sk, cb.ptr(comm.peers), comm.mine, comm.nbytes, comm.rank, comm.world,
+            cb.CEK_GEMV_EARLY_WEIGHTS if early_weights else 0, cb.current_stream())
 
 
 class DecodeChain:

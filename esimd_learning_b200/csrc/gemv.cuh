@@ -36,6 +36,11 @@ struct GemvParams {
   const unsigned long long* ar_peers;  // device array [ar_world] of comm base addresses
   unsigned* ar_sync;                   // this rank's sync block
   int ar_rank, ar_world;
+  // column-parallel all-gather epilogue (ag_n > 0, with ar_world ranks):
+  // this call computes rows [ag_row0, ag_row0 + N) of y [M, ag_n] and stores
+  // them at byte offset ag_off of the data area of every rank's comm region.
+  long long ag_off;
+  int ag_n, ag_row0;
   // several weight matrices sharing x in one launch (nmat > 0): matrix m
   // owns CTAs [mcta_off[m], mcta_off[m+1]) and writes ys[m] [M, ns[m]]
   int nmat;
@@ -68,6 +73,26 @@ CEK_DEVICE unsigned ld_acquire_sys(const unsigned* addr) {
 }
 
 // ---- device helpers shared by both GEMV kernels ----------------------------------
+
+// Output element (token tok, row n of this call) in one of three modes: a
+// local store, the all-reduce push (slot ar_rank of every rank's receive
+// buffer, slot set by the call's epoch parity), or the all-gather push (row
+// ag_row0 + n of every rank's full output).
+template <typename OutT>
+CEK_DEVICE void store_out(const GemvParams& p, OutT* y, int ldy, int tok, int n, OutT v) {
+  if (p.ar_world == 0) {
+    y[(size_t)tok * ldy + n] = v;
+  } else if (p.ag_n > 0) {
+    const size_t off = (size_t)tok * p.ag_n + p.ag_row0 + n;
+    for (int r = 0; r < p.ar_world; ++r)
+      reinterpret_cast<OutT*>(p.ar_peers[r] + tp::kSyncBytes + p.ag_off)[off] = v;
+  } else {
+    const unsigned set = (*reinterpret_cast<volatile unsigned*>(&p.ar_sync[tp::kEpoch]) + 1) & 1u;
+    const size_t off = (((size_t)set * p.ar_world + p.ar_rank) * p.M + tok) * p.N + n;
+    for (int r = 0; r < p.ar_world; ++r)
+      reinterpret_cast<OutT*>(p.ar_peers[r] + tp::kSyncBytes)[off] = v;
+  }
+}
 
 template <typename InT>
 CEK_DEVICE void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);

@@ -218,17 +218,7 @@ gemv_fp8_kernel(const GemvParams pin) {
     float s = 0.f;
     for (int q = 0; q < p.ks; ++q) s += red[rgl * p.ks + q][r][tl];
     s *= load_scale<SCALE>(p.scale, n);
-    if (p.ar_world == 0) {
-      reinterpret_cast<OutT*>(p.y)[(size_t)tok * p.N + n] = from_f32<OutT>(s);
-    } else {
-      // push this element into slot ar_rank of every rank's receive buffer
-      // (slot set by the parity of this call's epoch)
-      const OutT v = from_f32<OutT>(s);
-      const unsigned set = (*reinterpret_cast<volatile unsigned*>(&p.ar_sync[tp::kEpoch]) + 1) & 1u;
-      const size_t off = (((size_t)set * p.ar_world + p.ar_rank) * p.M + tok) * p.N + n;
-      for (int r = 0; r < p.ar_world; ++r)
-        reinterpret_cast<OutT*>(p.ar_peers[r] + tp::kSyncBytes)[off] = v;
-    }
+    store_out<OutT>(p, reinterpret_cast<OutT*>(p.y), p.N, tok, n, from_f32<OutT>(s));
   }
 }
 

@@ -438,17 +438,8 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
           for (int q = 0; q < kConsumers; ++q) u += rd[q][row + 8][tok];
           o = gelu_mul1<OutT>(o, from_f32<OutT>(u * out_scale_up));
         }
-        if (p.ar_world == 0) {
-          const int nm = p.nmat ? p.mns[bm] : p.N;
-          reinterpret_cast<OutT*>(p.nmat ? p.mys[bm] : p.y)[(size_t)tok * nm + out_row] = o;
-        } else {
-          // tensor-parallel push (tp_allreduce.cu): slot ar_rank of every
-          // rank's receive buffer, slot set chosen by this call's epoch parity
-          const unsigned set = (*reinterpret_cast<volatile unsigned*>(&p.ar_sync[tp::kEpoch]) + 1) & 1u;
-          const size_t off = (((size_t)set * p.ar_world + p.ar_rank) * p.M + tok) * p.N + out_row;
-          for (int r = 0; r < p.ar_world; ++r)
-            reinterpret_cast<OutT*>(p.ar_peers[r] + tp::kSyncBytes)[off] = o;
-        }
+        store_out<OutT>(p, reinterpret_cast<OutT*>(p.nmat ? p.mys[bm] : p.y), p.nmat ? p.mns[bm] : p.N, tok,
+                        out_row, o);
       }
     }
   }

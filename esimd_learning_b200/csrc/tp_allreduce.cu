@@ -79,6 +79,24 @@ tp_reduce_kernel(const unsigned long long* peers, unsigned* sync, T* out, int mn
   }
 }
 
+// Barrier over the ranks' comm regions: once every earlier kernel on this
+// stream has completed (griddepcontrol.wait), one fence at system scope, this
+// rank's ready flag raised on every rank with the call's epoch, a bounded
+// wait for every rank's flag, the epoch advanced.  After it, every push made
+// by any rank before its own barrier is visible here.
+__global__ void __launch_bounds__(32) tp_barrier_kernel(const unsigned long long* peers, unsigned* sync, int rank,
+                                                       int world) {
+  pdl_wait();
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(&sync[kEpoch]) + 1;
+  for (int r = threadIdx.x; r < world; r += 32) {
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<unsigned*>(peers[r]) + kReady + rank, e);
+  }
+  for (int r = threadIdx.x; r < world; r += 32) wait_at_least(&sync[kReady + r], e, &sync[kErrors]);
+  __syncwarp();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(&sync[kEpoch]) = e;
+}
+
 }  // namespace tp
 }  // namespace cek
 
@@ -190,4 +208,51 @@ extern "C" int cek_gemv_fp8_allreduce(const void* x, const void* w, const void* 
                            static_cast<__nv_bfloat16*>(out), mn, rank, world);
   if (e != cudaSuccess) return CEK_ERR_LAUNCH;
   return launch_status();
+}
+
+extern "C" int cek_comm_barrier(const uint64_t* peer_comm, void* my_comm, int rank, int world, void* stream) {
+  if (!peer_comm || !my_comm || world < 1 || world > cek::tp::kMaxRanks || rank < 0 || rank >= world)
+    return CEK_ERR_INVALID_ARG;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, cek::tp::tp_barrier_kernel, reinterpret_cast<const unsigned long long*>(peer_comm),
+                         static_cast<unsigned*>(my_comm), rank, world) != cudaSuccess)
+    return CEK_ERR_LAUNCH;
+  return cek_host::launch_status();
+}
+
+extern "C" int cek_gemv_fp8_allgather(const void* x, const void* w, const void* scale, int64_t M, int64_t N,
+                                      int64_t K, int64_t row0, int64_t n_full, int64_t y_off, int dtype, int w_fmt,
+                                      int scale_kind, const uint64_t* peer_comm, void* my_comm, int64_t comm_bytes,
+                                      int rank, int world, unsigned flags, void* stream) {
+  using namespace cek_host;
+  if (M <= 0 || N <= 0 || K <= 0 || K % 16 != 0 || row0 < 0 || row0 + N > n_full) return CEK_ERR_INVALID_ARG;
+  if (dtype != CEK_F16 && dtype != CEK_BF16) return CEK_ERR_INVALID_ARG;
+  if (w_fmt != CEK_E4M3 && w_fmt != CEK_E5M2) return CEK_ERR_INVALID_ARG;
+  if (scale_kind < CEK_SCALE_PERN_F16 || scale_kind > CEK_SCALE_PERT_F32) return CEK_ERR_INVALID_ARG;
+  if (flags & ~(unsigned)CEK_GEMV_EARLY_WEIGHTS) return CEK_ERR_INVALID_ARG;
+  if (world < 1 || world > cek::tp::kMaxRanks || rank < 0 || rank >= world) return CEK_ERR_INVALID_ARG;
+  if (y_off < 0 || y_off % 2 != 0 || n_full > INT32_MAX || M * n_full > INT32_MAX) return CEK_ERR_INVALID_ARG;
+  if ((int64_t)cek::tp::kSyncBytes + y_off + M * n_full * 2 > comm_bytes) return CEK_ERR_INVALID_ARG;
+  if (!x || !w || !scale || !peer_comm || !my_comm) return CEK_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(my_comm)) return CEK_ERR_ALIGNMENT;
+  cek::GemvParams p = {};
+  p.x = x; p.w = static_cast<const uint8_t*>(w); p.scale = scale; p.y = nullptr;
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.early_weights = (flags & CEK_GEMV_EARLY_WEIGHTS) ? 1 : 0;
+  p.ar_peers = reinterpret_cast<const unsigned long long*>(peer_comm);
+  p.ar_sync = static_cast<unsigned*>(my_comm);
+  p.ar_rank = rank;
+  p.ar_world = world;
+  p.ag_off = y_off;
+  p.ag_n = (int)n_full;
+  p.ag_row0 = (int)row0;
+  return cek::gemv_launch(p, dtype, dtype, w_fmt, scale_kind, false, static_cast<cudaStream_t>(stream));
 }

@@ -229,6 +229,25 @@ CEK_API int cek_ipc_open_handle(const void* handle, void** ptr);
 CEK_API int cek_ipc_close_handle(void* ptr);
 CEK_API int cek_comm_errors(void* my_comm, uint32_t* out);
 CEK_API int cek_comm_reset(void* my_comm, int64_t bytes);
+/* ---- tensor parallel: column-parallel FP8 GEMV fused with its all-gather --
+ * This rank holds rows [row0, row0 + N) of the weight (and their scales) and
+ * computes those rows of y [M, n_full] = x @ deq(W)^T * scale; the epilogue
+ * stores them over NVLink into every rank's copy of y, which sits at byte
+ * offset y_off of the data area (CEK_COMM_SYNC_BYTES into the region) of
+ * each rank's comm region (comm_bytes long, set up as for the all-reduce).
+ * No barrier inside: after the step's all-gather GEMVs, cek_comm_barrier on
+ * every rank makes all ranks' rows visible everywhere.  A y buffer must not
+ * be written by the next call before every rank has finished reading it
+ * (alternate two buffers by step parity).  Replaces the NCCL all-gather that
+ * follows a column-parallel GEMV; no reference counterpart (single-GPU). */
+#define CEK_COMM_SYNC_BYTES 4096
+CEK_API int cek_gemv_fp8_allgather(const void* x, const void* w, const void* scale, int64_t M, int64_t N,
+                                   int64_t K, int64_t row0, int64_t n_full, int64_t y_off, int dtype,
+                                   int w_fmt, int scale_kind, const uint64_t* peer_comm, void* my_comm,
+                                   int64_t comm_bytes, int rank, int world, unsigned flags, void* stream);
+/* Barrier over the comm regions of all ranks, on the stream after the
+ * pushes it covers (one bounded wait; a timeout sets the error word). */
+CEK_API int cek_comm_barrier(const uint64_t* peer_comm, void* my_comm, int rank, int world, void* stream);
 CEK_API int cek_gemv_fp8_allreduce(const void* x, const void* w, const void* scale, void* out,
                                    int64_t M, int64_t N, int64_t K, int dtype, int w_fmt,
                                    int scale_kind, const uint64_t* peer_comm, void* my_comm,

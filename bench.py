@@ -180,14 +180,29 @@ def workloads():
     return mod
 
 
+def n_sets_for(world: int) -> int:
+    """Weight sets rotated between steps so that > 3x L2 (126 MB) of weights
+    pass through each GPU before a set is read again."""
+    per_rank = sum(N * K for _, N, K in SHAPES) / world
+    return 2 if world == 1 else max(2, -(-(3 * 126 * 2**20) // int(per_rank)))
+
+
 def arm_config(world: int, prefetch: bool) -> dict:
     """The `config` object of the JSON line; both arms print exactly this."""
+    if world == 1:
+        return {"workload": "BASELINE config 1: batched FP8 GEMV, per-channel fp32 scales",
+                "shapes": {n: [N, K] for n, N, K in SHAPES}, "M": MS,
+                "l2": "2 weight sets alternating with M: > 126 MB (L2) between two reads of one weight",
+                "timing": "CUDA graph of the 12 launches per step, CUDA events",
+                "weight_prefetch": prefetch, "parallelism": "single GPU"}
     return {"workload": "BASELINE config 1: batched FP8 GEMV, per-channel fp32 scales",
             "shapes": {n: [N, K] for n, N, K in SHAPES}, "M": MS,
-            "l2": "2 weight sets alternating with M: > 126 MB (L2) between two reads of one weight",
-            "timing": "CUDA graph of the 12 launches per step, CUDA events",
+            "l2": f"{n_sets_for(world)} weight sets per rank rotated: > 3x L2 between two reads of one weight",
+            "timing": "CUDA graph of the steps (12 launches + 1 barrier each), CUDA events, max over ranks",
             "weight_prefetch": prefetch,
-            "parallelism": f"replicas x{world} (independent GEMV sweeps)"}
+            "parallelism": f"column-parallel x{world}: each rank streams N/{world} rows of every weight and "
+                           "pushes its rows into every rank's full output over NVLink in the GEMV epilogue "
+                           "(cek_gemv_fp8_allgather), one barrier per step"}
 
 
 def build_sets(dev, n_sets: int = 2):
@@ -217,6 +232,134 @@ def build_sets(dev, n_sets: int = 2):
         yo += yn
     xs["_buf"], ys["_buf"] = xbuf, ybuf
     return sets, xs, ys
+
+
+def run_ours_tp(args, rank, world, local):
+    """N > 1: the same config-1 step, strong-scaled.  Every GEMV is
+    column-parallel over the ranks (rows [N r / W, N (r + 1) / W) of each
+    weight on rank r) and its all-gather is fused into the epilogue: each
+    rank stores its rows into every rank's copy of the full output over
+    NVLink peer memory; one barrier ends the step.  value = the step's
+    algorithmic bytes (counted once for the whole job) / max-over-ranks time."""
+    import esimd_learning_b200 as ops
+    from esimd_learning_b200.chain import TPComm, gemv_fp8_allgather, shard_rows
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    W = workloads()
+    prefetch = not args.no_prefetch
+    nsets = n_sets_for(world)
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    sets = []
+    for _ in range(nsets):
+        ws = {}
+        for name, N, K in SHAPES:
+            r0, r1 = shard_rows(N, rank, world)
+            ws[name] = W.quantize_per_channel(torch.randn(r1 - r0, K, device=dev, generator=gen) * 0.02) + (r0,)
+        sets.append(ws)
+    g0 = torch.Generator().manual_seed(0)
+    xsz = [M * K for (_, N, K, M) in CALLS]
+    xbuf = torch.randn(sum(xsz), generator=g0).to(torch.float16).to(dev)
+    xs, o = {}, 0
+    for (name, N, K, M), n in zip(CALLS, xsz):
+        xs[(name, M)] = xbuf[o:o + n].view(M, K)
+        o += n
+    ysz = [M * N * 2 for (_, N, K, M) in CALLS]
+    yoff = [sum(ysz[:i]) for i in range(len(CALLS))]
+    ytotal = (sum(ysz) + 255) // 256 * 256
+    comm = TPComm(0, rank, world, dev, data_bytes=2 * ytotal)
+
+    def step(si):
+        ws = sets[si % nsets]
+        for ci, (name, N, K, M) in enumerate(CALLS):
+            w, sc, r0 = ws[name]
+            gemv_fp8_allgather(comm, xs[(name, M)], w, sc, r0, N, (si % 2) * ytotal + yoff[ci],
+                               early_weights=prefetch)
+        comm.barrier()
+
+    graph_steps = nsets if nsets % 2 == 0 else 2 * nsets
+    st = torch.cuda.Stream(dev)
+    with torch.cuda.stream(st):
+        step(0)
+        torch.cuda.synchronize()
+        barrier(world)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for si in range(graph_steps):
+                step(si)
+    torch.cuda.synchronize()
+    replays = max(1, -(-args.steps // graph_steps))
+    steps = replays * graph_steps
+    with torch.cuda.stream(st):
+        for _ in range(max(1, -(-args.warmup // graph_steps))):
+            graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            for _ in range(replays):
+                graph.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_step = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    value = STEP_BYTES / (ms_step * 1e-3) / 1e9
+
+    # e2e through the public API (chain.gemv_fp8_allgather + barrier), eager:
+    # the step's activations copied host->device, the gathered outputs read back
+    hx = xbuf.cpu().pin_memory()
+    yview = comm.data_tensor(0, (sum(ysz) // 2,))
+    hy = torch.empty(yview.shape, dtype=torch.float16).pin_memory()
+    e2e_steps = max(3, min(args.steps, 300))
+    with torch.cuda.stream(st):
+        def e2e_step():
+            xbuf.copy_(hx, non_blocking=True)
+            step(0)
+            hy.copy_(yview, non_blocking=True)
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(st)
+        for _ in range(e2e_steps):
+            e2e_step()
+        a1.record(st)
+        torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(a0.elapsed_time(a1), world) / e2e_steps
+    errors = comm.errors()
+    peak, peak_kind = peaks()
+    per_gpu = STEP_BYTES / world / (ms_step * 1e-3) / 1e9
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "e4m3*fp16->fp32", "data": "synthetic (seeded: x~N(0,1) fp16, W~N(0,0.02) per-row e4m3)",
+        "config": arm_config(world, prefetch),
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(per_gpu / peak, 4), "peak_source": peak_kind, "traffic": None,
+                     "algorithmic_bytes": STEP_BYTES // world,
+                     "kernel": "cek::bulk::gemv_bulk_kernel with the all-gather push epilogue (per GPU: "
+                               "its share of the step's bytes / step time)"},
+        "e2e": {"value": round(STEP_BYTES / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
+                "ms_per_step": round(e2e_ms, 5),
+                "api": "esimd_learning_b200.chain.gemv_fp8_allgather + TPComm.barrier, eager"},
+        "gpu_launches": (len(CALLS) + 1) * steps,
+        "clocks": clk.summary(),
+        "comm_errors": errors,
+    }
+    del graph
+    comm.close()
+    torch.cuda.empty_cache()
+    if not args.no_chain:
+        out["chain"] = measure_chain(dev, rank, world)
+    return out
 
 
 def run_ours(args, rank, world, local):
@@ -347,6 +490,7 @@ def run_ours(args, rank, world, local):
         "clocks": clk.summary(),
     }
     out["config0"] = measure_config0(dev)
+    out["config2"] = measure_config2(dev)
     if not args.no_gemm:
         out["gemm"] = {f"M{M}": measure_gemm(dev, M) for M in (2048, 8192)}
     if not args.no_chain:
@@ -551,6 +695,57 @@ def measure_config0(dev, reps: int = 240) -> dict:
     return {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
             "frac": round(b / (us * 1e-6) / 1e9 / peak, 4), "peak_gbs": peak, "peak_source": src,
             "algorithmic_bytes": b, "timing": "CUDA graph of back-to-back calls, 32 rotating weight copies"}
+
+
+def measure_config2(dev, reps_per_copy: int = 4) -> dict:
+    """fused residual add + RMSNorm -> QKV GEMV [6144, 4096]
+    (esimd_fused_add_rms_norm_batched_fp8) at M = 1, 2, 4, 8, against the
+    plain GEMV on the same weights.  CUDA graph of back-to-back calls over
+    rotating weight copies (> 4x L2); CUDA events; per-call mean.  Bytes:
+    N K + 4 N (scales) + 6 M K (read h, r; write r) + 2 K (gamma) + 2 M N."""
+    import esimd_learning_b200 as ops
+    N, K = 6144, 4096
+    gen = torch.Generator(device=dev).manual_seed(5)
+    ncopy = -(-(512 << 20) // (N * K))
+    copies = [torch.randint(0, 120, (N, K), dtype=torch.uint8, device=dev, generator=gen)
+              .view(torch.float8_e4m3fn) for _ in range(ncopy)]
+    sc = torch.rand(N, device=dev, generator=gen) * 0.01 + 1e-3
+    gamma = (1 + 0.1 * torch.randn(K, device=dev, generator=gen)).half()
+    st = torch.cuda.Stream(dev)
+    peak, src = peaks()
+
+    def graph_us(fn, reps):
+        with torch.cuda.stream(st):
+            fn(0)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                for r in range(reps):
+                    fn(r)
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            g.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    res = {"shape": [N, K], "timing": "CUDA graph of back-to-back calls, rotating weight copies", "peak_gbs": peak,
+           "peak_source": src}
+    for M in (1, 2, 4, 8):
+        h = torch.randn(M, K, device=dev, generator=gen).half()
+        r = torch.randn(M, K, device=dev, generator=gen).half()
+        y = torch.empty(M, N, device=dev, dtype=torch.float16)
+        fused = graph_us(lambda i: ops.esimd_fused_add_rms_norm_batched_fp8(h, r, gamma, 1e-6, copies[i % ncopy], sc, y),
+                         reps_per_copy * ncopy)
+        plain = graph_us(lambda i: ops.esimd_gemv_fp8_pern(h, copies[i % ncopy], sc, y, N, K), reps_per_copy * ncopy)
+        b = N * K + 4 * N + 6 * M * K + 2 * K + 2 * M * N
+        res[f"M{M}"] = {"fused_us": round(fused, 3), "plain_gemv_us": round(plain, 3),
+                        "gbs": round(b / (fused * 1e-6) / 1e9, 1), "frac": round(b / (fused * 1e-6) / 1e9 / peak, 4)}
+    del copies
+    torch.cuda.empty_cache()
+    return res
 
 
 def measure_gemm(dev, M: int, reps: int = 20) -> dict:
@@ -793,7 +988,7 @@ def main():
             print(json.dumps(out), file=out_file, flush=True)
         return
     rank, world, local = dist_init(args.gpus)
-    out = run_ours(args, rank, world, local)
+    out = run_ours(args, rank, world, local) if world == 1 else run_ours_tp(args, rank, world, local)
     if rank == 0:
         print(json.dumps(out), file=out_file, flush=True)
     if world > 1:

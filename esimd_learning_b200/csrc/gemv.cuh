@@ -30,6 +30,14 @@ struct GemvParams {
   // [N, 2N) (scale likewise); y [M, N] = io(gelu_tanh(io(gate)) * io(up))
   // (bulk kernel only)
   int y_gelu;
+  // 1: residual add + RMSNorm prologue inside the bulk GEMV.  x is the
+  // hidden state, residual the OLD residual (only read here), gamma the
+  // pre-shifted norm weight; every CTA forms io(f32(io(h + r)) * inv_rms *
+  // gamma) on chip (shared or tensor memory), inv_rms from the unrounded
+  // h + r.  The CTAs trigger their dependents only after their last read of
+  // the residual, so a kernel launched behind them may update it in place.
+  int norm;
+  float eps;
   // tensor-parallel all-reduce epilogue (ar_world > 0, tp_allreduce.cu):
   // y is pushed into slot ar_rank of every rank's receive buffer instead of
   // being stored to p.y.

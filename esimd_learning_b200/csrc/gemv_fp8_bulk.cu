@@ -124,7 +124,8 @@ CEK_DEVICE int count_blocks(const GemvParams& p, int r0, int r1, int bsz) {
 }
 
 // NT: 8-token groups (the n8 columns of the MMA), 1 for M <= 8, 2 for M <= 16.
-template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT>
+// NORM: the residual add + RMSNorm prologue (GemvParams::norm).
+template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -153,7 +154,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     mbar::fence_init();
   }
   __syncthreads();
-  pdl_launch_dependents();
+  if constexpr (!NORM) pdl_launch_dependents();
 #ifdef CEK_BULK_TRACE
   __shared__ unsigned trace_slot;
   if (threadIdx.x == 0) {
@@ -208,7 +209,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       for (int i = 0; i < pre; ++i) issue(i);
     pdl_wait();
     if (lane == 0) TRACE(tslot, 3);
-    if (XM == kXSmem && lane == 0) {
+    if (XM == kXSmem && lane == 0 && !NORM) {
       const uint32_t xb = (uint32_t)p.M * (uint32_t)K * 2u;
       const uint32_t bar = mbar::saddr(&xbar);
       mbar::arrive_expect_tx(bar, xb);
@@ -264,6 +265,87 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   // slabs requested early, so until it lands the slabs use the global path.
   pdl_wait();
   bool x_smem = false;
+  // Norm prologue, pass 1 (all consumer threads, token by token): the sum of
+  // squares of the unrounded h + r, reduced over the CTA into the inverse
+  // RMS; with x in shared memory the rounded residual io(h + r) is stored
+  // there on the way.
+  __shared__ float ninv[NORM ? 16 : 1];
+  __shared__ float nred[NORM ? kConsumers : 1][NORM ? 16 : 1];
+  if constexpr (NORM) {
+    const int nvec = K >> 3;
+#pragma unroll 2
+    for (int m = 0; m < p.M; ++m) {
+      const uint4* hv = reinterpret_cast<const uint4*>(static_cast<const InT*>(p.x) + (size_t)m * K);
+      const uint4* rv = reinterpret_cast<const uint4*>(static_cast<const InT*>(p.residual) + (size_t)m * K);
+      float ss = 0.f;
+#pragma unroll 4
+      for (int v = ctid; v < nvec; v += kConsumers * 32) {
+        const uint4 h = ldg_nc(hv + v), r = ldg_nc(rv + v);
+        const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, rw[4] = {r.x, r.y, r.z, r.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 hf = unpack2<InT>(hw[q]), rf = unpack2<InT>(rw[q]);
+          const float a = hf.x + rf.x, b = hf.y + rf.y;
+          ss += a * a + b * b;
+          o[q] = pack2<InT>(a, b);
+        }
+        if (XM == kXSmem) reinterpret_cast<uint4*>(smem + (size_t)m * K * 2)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) nred[cw][m] = ss;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    if (ctid < p.M) {
+      float t = 0.f;
+#pragma unroll
+      for (int q = 0; q < kConsumers; ++q) t += nred[q][ctid];
+      ninv[ctid] = rsqrtf(t / (float)K + p.eps);
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+  }
+  // pass 2 helper (x in tensor memory): the 16 normalised activations of
+  // token tok at k .. k + 15, io(f32(io(h + r)) * inv_rms * gamma), the
+  // rounding points of the two-kernel path
+  auto norm16 = [&](int tok, int k, uint4& a, uint4& b) {
+    const InT* hp = static_cast<const InT*>(p.x) + (size_t)tok * K + k;
+    const InT* rp = static_cast<const InT*>(p.residual) + (size_t)tok * K + k;
+    const InT* gp = static_cast<const InT*>(p.gamma) + k;
+    const float inv = ninv[tok];
+    uint32_t o[8];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint4 h = ldg_nc(hp + 8 * half), r = ldg_nc(rp + 8 * half), gm = ldg_nc(gp + 8 * half);
+      const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, rw[4] = {r.x, r.y, r.z, r.w}, gw[4] = {gm.x, gm.y, gm.z, gm.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 hf = unpack2<InT>(hw[q]), rf = unpack2<InT>(rw[q]), gf = unpack2<InT>(gw[q]);
+        const float2 res = unpack2<InT>(pack2<InT>(hf.x + rf.x, hf.y + rf.y));
+        o[4 * half + q] = pack2<InT>(res.x * inv * gf.x, res.y * inv * gf.y);
+      }
+    }
+    a = make_uint4(o[0], o[1], o[2], o[3]);
+    b = make_uint4(o[4], o[5], o[6], o[7]);
+  };
+  if (XM == kXSmem && NORM) {
+    // pass 2 in place: x[m][k] = io(x[m][k] * inv_rms[m] * gamma[k])
+    const int nvec = K >> 3;
+    for (int e = ctid; e < p.M * nvec; e += kConsumers * 32) {
+      const int m = e / nvec, v = e - m * nvec;
+      uint4* xp = reinterpret_cast<uint4*>(smem + (size_t)m * K * 2) + v;
+      const uint4 x4 = *xp, gm = ldg_nc(static_cast<const InT*>(p.gamma) + 8 * v);
+      const uint32_t xw[4] = {x4.x, x4.y, x4.z, x4.w}, gw[4] = {gm.x, gm.y, gm.z, gm.w};
+      const float inv = ninv[m];
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 xf = unpack2<InT>(xw[q]), gf = unpack2<InT>(gw[q]);
+        o[q] = pack2<InT>(xf.x * inv * gf.x, xf.y * inv * gf.y);
+      }
+      *xp = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    x_smem = true;  // visible to all consumers after the barrier below
+  }
   // tensor-memory copy of x: warp cw owns global chunks cw, cw + 8, ...; its
   // chunk j sits in columns [8 NT j, 8 NT (j + 1)) of its half of its lane
   // quadrant (warps cw and cw + 4 share the quadrant of warp index % 4),
@@ -280,17 +362,46 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     xt = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (cw >= 4 ? kTmemCols / 2 : 0);
-    for (int j = 0; cw + j * kConsumers < K / 64; ++j) {
+    if constexpr (!NORM) {
+      for (int j = 0; cw + j * kConsumers < K / 64; ++j) {
 #pragma unroll
-      for (int u = 0; u < NT; ++u) {
-        const InT* xq = xglob[u] + 64 * (cw + j * kConsumers);
-        const uint4 a = ldg_nc(xq), b = ldg_nc(xq + 8);
-        asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
-                     ::"r"(xt + 8u * (NT * j + u)), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y),
-                     "r"(b.z), "r"(b.w) : "memory");
+        for (int u = 0; u < NT; ++u) {
+          const InT* xq = xglob[u] + 64 * (cw + j * kConsumers);
+          const uint4 a = ldg_nc(xq), b = ldg_nc(xq + 8);
+          asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                       ::"r"(xt + 8u * (NT * j + u)), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y),
+                         "r"(b.z), "r"(b.w) : "memory");
+        }
+      }
+    } else {
+      // two chunks per batch: all their loads issue before the first store
+      const int nj = (K / 64 - cw + kConsumers - 1) / kConsumers;
+      for (int j0 = 0; j0 < nj; j0 += 2) {
+        uint4 a[2][NT], b[2][NT];
+#pragma unroll
+        for (int v = 0; v < 2; ++v)
+#pragma unroll
+          for (int u = 0; u < NT; ++u)
+            norm16(g + 8 * u < p.M ? g + 8 * u : 0, 64 * (cw + min(j0 + v, nj - 1) * kConsumers) + 16 * t, a[v][u],
+                   b[v][u]);
+#pragma unroll
+        for (int v = 0; v < 2; ++v)
+#pragma unroll
+          for (int u = 0; u < NT; ++u)
+            if (j0 + v < nj)
+              asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                           ::"r"(xt + 8u * (NT * (j0 + v) + u)), "r"(a[v][u].x), "r"(a[v][u].y), "r"(a[v][u].z),
+                             "r"(a[v][u].w), "r"(b[v][u].x), "r"(b[v][u].y), "r"(b[v][u].z), "r"(b[v][u].w)
+                           : "memory");
       }
     }
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+  }
+  // the residual has been read for the last time: a kernel launched behind
+  // this one may now update it in place
+  if constexpr (NORM) {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    pdl_launch_dependents();
   }
   if (cw == 0 && lane == 0) TRACE(tslot, 5);
 
@@ -522,9 +633,9 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   return pl;
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT>
+template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM = false>
 int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
-  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM, NT>;
+  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM, NT, NORM>;
   static cek_host::DeviceSlots configured_smem;
   constexpr int kMaxDyn = kSmemBudget - (NT - 1) * 8 * 1024;  // beside the static reduction array
   if (!cek_host::ensure_smem_attr(configured_smem, kern, kMaxDyn)) return CEK_ERR_LAUNCH;
@@ -543,6 +654,9 @@ int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
 
 template <typename InT, int F, int S, typename OutT, int NT>
 int launch_x(const GemvParams& p, const Plan& pl, cudaStream_t st) {
+  // the norm prologue (e4m3 weights only) keeps x in shared or tensor memory
+  if constexpr (F == CEK_E4M3)
+    if (p.norm) return launch<InT, F, S, OutT, kXSmem, NT, true>(p, pl, st);
   return pl.xmode == kXSmem   ? launch<InT, F, S, OutT, kXSmem, NT>(p, pl, st)
          : pl.xmode == kXTmem ? launch<InT, F, S, OutT, kXTmem, NT>(p, pl, st)
                               : launch<InT, F, S, OutT, kXL2, NT>(p, pl, st);
@@ -577,6 +691,12 @@ int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, i
   if (disabled) return CEK_ERR_UNSUPPORTED;
   const bulk::Plan pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K);
   if (pl.stages == 0 || (p.y_gelu && (p.nmat || p.ar_world))) return CEK_ERR_UNSUPPORTED;
+  // the norm prologue needs x on chip and a single plain or gated matrix
+  // The norm prologue runs where x fits in shared memory beside the ring (one
+  // pass over h + r stores the residual there).  With x in tensor memory
+  // (M >= 4 at K = 4096) it measured slower than the two-kernel path, which
+  // the caller then takes.
+  if (p.norm && (pl.xmode != bulk::kXSmem || p.nmat || p.ar_world || w_fmt != CEK_E4M3)) return CEK_ERR_UNSUPPORTED;
   // two token groups with x from L2 measured slower than the split-K kernel
   // (down 4096 x 14336 at M = 16: 24.3 against 22.5 us)
   if (pl.nt == 2 && pl.xmode == bulk::kXL2 && !p.y_gelu) return CEK_ERR_UNSUPPORTED;

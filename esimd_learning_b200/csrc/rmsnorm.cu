@@ -123,6 +123,65 @@ static int launch_norm(void* hidden, void* residual, const void* weight, float* 
   return CEK_ERR_INVALID_ARG;
 }
 
+// residual = io(hidden + residual), launched behind the bulk GEMV with the
+// norm prologue.  It may start once every GEMV CTA has read the residual for
+// the last time (their programmatic-launch trigger); it triggers its own
+// dependents at once and waits for the GEMV's completion before it exits, so
+// the next kernel's griddepcontrol.wait covers both.
+template <typename T>
+__global__ void __launch_bounds__(256) residual_update_kernel(const T* __restrict__ hidden, T* residual, int nvec) {
+  pdl_launch_dependents();
+  const uint4* hv = reinterpret_cast<const uint4*>(hidden);
+  uint4* rv = reinterpret_cast<uint4*>(residual);
+  for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += gridDim.x * blockDim.x) {
+    const uint4 h = hv[v], r = rv[v];
+    const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, rw[4] = {r.x, r.y, r.z, r.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 hf = unpack2<T>(hw[q]), rf = unpack2<T>(rw[q]);
+      o[q] = pack2<T>(hf.x + rf.x, hf.y + rf.y);
+    }
+    rv[v] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  pdl_wait();
+}
+
+// The one-pass fused op: the bulk GEMV forms the normalised rows on chip
+// (GemvParams::norm), then residual_update_kernel writes the residual.  No
+// scratch memory.  CEK_ERR_UNSUPPORTED when the bulk GEMV cannot hold x on
+// chip for this shape (the caller then takes the two-kernel path).
+template <typename T>
+int fused_norm_gemv_onchip(const void* hidden, void* residual, const void* gamma, float eps, GemvParams p,
+                           int dtype, int w_fmt, int scale_kind, cudaStream_t st) {
+  static const bool off = [] {
+    const char* v = std::getenv("CEK_FUSED_NORM_PROLOGUE");
+    return v && v[0] == '0';
+  }();
+  if (off) return CEK_ERR_UNSUPPORTED;
+  p.x = hidden;
+  p.residual = residual;
+  p.gamma = gamma;
+  p.norm = 1;
+  p.eps = eps;
+  int s = gemv_bulk_launch(p, dtype, dtype, w_fmt, scale_kind, st);
+  if (s != CEK_OK) return s;
+  const int nvec = p.M * p.K / 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::min(148, (nvec + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, residual_update_kernel<T>, static_cast<const T*>(hidden), static_cast<T*>(residual),
+                         nvec) != cudaSuccess)
+    return CEK_ERR_LAUNCH;
+  return cek_host::launch_status();
+}
+
 }  // namespace cek
 
 namespace {
@@ -185,6 +244,18 @@ extern "C" int cek_fused_add_rmsnorm_gemv_fp8(const void* hidden, void* residual
   if (!cek_host::aligned16(norm_weight) || !cek_host::aligned16(w) || !cek_host::aligned16(workspace))
     return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N > 0 && K % 64 == 0) {
+    cek::GemvParams q = {};
+    q.w = static_cast<const uint8_t*>(w); q.scale = scale; q.y = y;
+    q.M = (int)M; q.N = (int)N; q.K = (int)K;
+    q.early_weights = 1;  // nothing in front of the GEMV writes W
+    q.y_gelu = gelu_out ? 1 : 0;
+    s = dtype == CEK_F16
+            ? cek::fused_norm_gemv_onchip<__half>(hidden, residual, norm_weight, eps, q, dtype, w_fmt, scale_kind, st)
+            : cek::fused_norm_gemv_onchip<__nv_bfloat16>(hidden, residual, norm_weight, eps, q, dtype, w_fmt,
+                                                         scale_kind, st);
+    if (s != CEK_ERR_UNSUPPORTED) return s;
+  }
   const bool staged = workspace_bytes >= normed_bytes(M, K);
   float* inv = static_cast<float*>(workspace);
   // The stats kernel only reads `hidden`; the const_cast never leads to a write.

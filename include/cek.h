@@ -113,10 +113,16 @@ CEK_API int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* weig
  * residual = io(hidden + residual)  (in place; hidden is not written)
  * xn       = io(f32(residual) * inv_rms[m] * weight)
  * y        = GEMV(xn, w, scale)  as cek_gemv_fp8.
- * Two launches chained by programmatic dependent launch: a per-row stats
- * kernel (residual update and normalisation) and the GEMV, which streams w
- * while the stats kernel runs.
- * workspace (contents ignored):
+ * Where x [M, K] fits in the bulk GEMV's shared memory beside its weight
+ * ring (M <= 2 at K = 4096, M = 1 at K = 8192; e4m3 weights, K % 64 == 0)
+ * the GEMV itself forms xn on chip: every CTA reads hidden and residual,
+ * reduces the inverse RMS and stages xn, then a small kernel launched
+ * behind it (once all CTAs have read the residual) writes the residual.
+ * The workspace is not touched there.  Otherwise two launches chained by
+ * programmatic dependent launch: a per-row stats kernel (residual update
+ * and normalisation) and the GEMV, which streams w while the stats kernel
+ * runs.
+ * workspace (contents ignored; required either way):
  *   >= cek_fused_add_rmsnorm_gemv_fp8_workspace_bytes(M, K) bytes: the stats
  *      kernel writes xn there (M x K, L2-resident) and the GEMV reads it;
  *   >= 256 bytes only: the stats kernel writes the per-row inverse RMS and

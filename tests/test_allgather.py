@@ -130,7 +130,10 @@ def test_allgather_two_gpus():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     worker = Path(__file__).resolve().parent / "allgather_worker.py"
-    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-                        "--master-addr", "127.0.0.1", "--master-port", str(_port()), str(worker)],
-                       capture_output=True, text=True, timeout=600, env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
+    for _ in range(3):  # a free port can be taken between the probe and the rendezvous: retry
+        r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                            "--master-addr", "127.0.0.1", "--master-port", str(_port()), str(worker)],
+                           capture_output=True, text=True, timeout=600, env={**os.environ, "NCCL_NVLS_ENABLE": "0"})
+        if "EADDRINUSE" not in r.stderr:
+            break
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]

@@ -525,10 +525,12 @@ extern "C" int cek_gemm_fp8w(const void* x, const void* w, const void* scale, vo
   if (M == 0 || N == 0) return CEK_OK;
   if (K == 0 || K % 64 != 0 || N % 16 != 0) return CEK_ERR_INVALID_ARG;
   if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2) return CEK_ERR_INVALID_ARG;
-  if (!x || !w || !scale || !y || !workspace) return CEK_ERR_INVALID_ARG;
-  if (workspace_bytes < cek_gemm_fp8w_workspace_bytes(N, K)) return CEK_ERR_INVALID_ARG;
+  // the workspace is used (and required) only above kGemmW8MaxRows tokens
+  const bool need_ws = M > kGemmW8MaxRows;
+  if (!x || !w || !scale || !y || (need_ws && !workspace)) return CEK_ERR_INVALID_ARG;
+  if (need_ws && workspace_bytes < cek_gemm_fp8w_workspace_bytes(N, K)) return CEK_ERR_INVALID_ARG;
   if (!cek_host::aligned16(x) || !cek_host::aligned16(w) || !cek_host::aligned16(y) ||
-      !cek_host::aligned16(workspace))
+      (need_ws && !cek_host::aligned16(workspace)))
     return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float* sc = static_cast<const float*>(scale);

@@ -24,6 +24,7 @@ from __future__ import annotations
 import torch
 
 GEMV_MAX_TOKENS = 64
+GEMM_W8_MAX_TOKENS = 256  # cek_gemm_fp8w converts weight tiles in shared memory up to this M
 
 
 class EsimdFp8LinearMethod:
@@ -75,10 +76,12 @@ class EsimdFp8LinearMethod:
         if M == 0:
             return y.reshape(*lead, N)
         if M > GEMV_MAX_TOKENS and K % 64 == 0 and N % 16 == 0:
-            nb = cabi.lib().cek_gemm_fp8w_workspace_bytes(N, K)
-            ws = torch.empty(nb, dtype=torch.uint8, device=x.device)
+            # the 16-bit weight copy is needed only above GEMM_W8_MAX_TOKENS
+            nb = cabi.lib().cek_gemm_fp8w_workspace_bytes(N, K) if M > GEMM_W8_MAX_TOKENS else 0
+            ws = torch.empty(nb, dtype=torch.uint8, device=x.device) if nb else None
             kind = cabi.CEK_SCALE_PERT_F32 if s.numel() == 1 else cabi.CEK_SCALE_PERN_F32
-            cabi.call("cek_gemm_fp8w", cabi.ptr(x2), cabi.ptr(w), cabi.ptr(s), cabi.ptr(y), cabi.ptr(ws), nb,
+            cabi.call("cek_gemm_fp8w", cabi.ptr(x2), cabi.ptr(w), cabi.ptr(s), cabi.ptr(y),
+                      cabi.ptr(ws) if ws is not None else None, nb,
                       M, N, K, cabi.io_dtype(x2), cabi.fp8_format(w), kind, cabi.current_stream())
         elif s.numel() == 1:
             ops.esimd_gemm_fp8_pert(x2, w, s.reshape(()), y)

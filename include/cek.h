@@ -282,7 +282,8 @@ CEK_API int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* a_s
  * dtype), then kind::f16 tcgen05 MMAs with fp32 accumulation; the scale
  * (fp32 per-tensor scalar, or fp32 per-N) is applied in the epilogue.
  * M <= 256: each weight tile is copied to shared memory as FP8 and
- * converted there by converter warps (workspace untouched).  M > 256: the
+ * converted there by converter warps (workspace untouched; it may be null
+ * with workspace_bytes 0).  M > 256: the
  * weight is dequantised once into `workspace`
  * (cek_gemm_fp8w_workspace_bytes(N, K) bytes), then the 16-bit GEMM runs.
  * x, y, T = dtype (CEK_F16 / CEK_BF16), row-major and contiguous.

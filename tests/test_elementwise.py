@@ -152,3 +152,32 @@ def test_gelu_mul_output_flag_cabi(cuda_device):
                             cabi.CEK_F16, cabi.CEK_E4M3, cabi.CEK_SCALE_PERN_F32, cabi.CEK_GEMV_GELU_MUL_OUTPUT,
                             cabi.current_stream())
         assert rc == cabi.CEK_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_quant_every_16bit_value_many_scales(ext, cuda_device, io):
+    """Every finite positive and negative 16-bit value, in rows whose amax
+    (and so scale) differ, against torch's IEEE division: the codes and the
+    scales must agree bit for bit."""
+    bits = torch.arange(0, 1 << 16, dtype=torch.int32).to(torch.int16)
+    vals = bits.view(io).float()
+    vals = vals[torch.isfinite(vals)]
+    K = 4096
+    vals = vals[: (vals.numel() // K) * K].reshape(-1, K)
+    g = torch.Generator().manual_seed(7)
+    rows = []
+    for i in range(vals.shape[0]):
+        r = vals[i].clone()
+        # a per-row amax drawn across 12 octaves, so the scales differ widely
+        amax = float(2.0 ** torch.randint(-6, 6, (1,), generator=g).item()) * (1 + torch.rand(1, generator=g).item())
+        r = torch.where(r.abs() > amax, torch.zeros_like(r), r)
+        r[0] = amax
+        rows.append(r)
+    a = torch.stack(rows).to(io)
+    M = a.shape[0]
+    q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=cuda_device)
+    s = torch.empty(M, dtype=torch.float32, device=cuda_device)
+    ext.esimd_quant_fp8_per_token(a.to(cuda_device), q, s)
+    rq, rs = O.quant_fp8_per_token(a)
+    assert torch.equal(s.cpu(), rs)
+    assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))

@@ -929,6 +929,19 @@ def profile_chain(M: int):
     print("profile chain done")
 
 
+def profile_config2(M: int):
+    """Two calls of the fused add+RMSNorm -> QKV GEMV of BASELINE config 2 at
+    this M ([6144, 4096] e4m3 weight, fp32 per-channel scales)."""
+    import esimd_learning_b200 as ops
+    dev = torch.device("cuda", 0)
+    h, r, g, wq, sc = (t.to(dev) for t in workloads().fused_norm_case(M))
+    y = torch.empty(M, 6144, dtype=torch.float16, device=dev)
+    for _ in range(2):
+        ops.esimd_fused_add_rms_norm_batched_fp8(h, r, g, 1e-6, wq, sc, y)
+    torch.cuda.synchronize()
+    print("profile config2 done")
+
+
 def profile_gemm(M: int):
     """Two launches each of the per-token quantisation and the tcgen05 GEMM of
     BASELINE config 3 at this M (A [M, 4096], B [14336, 4096])."""
@@ -962,6 +975,8 @@ def main():
     ap.add_argument("--vllm-compare", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--profile-chain", type=int, default=0, metavar="M",
                     help="run two eager TP=1 decode-chain steps (config 4) at this M and exit; for ncu")
+    ap.add_argument("--profile-config2", type=int, default=0, metavar="M",
+                    help="run the fused add+RMSNorm -> QKV GEMV of config 2 at this M twice and exit; for ncu")
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="M",
                     help="run quant + tcgen05 GEMM of config 3 at this M twice and exit; for ncu")
     ap.add_argument("--profile", action="store_true",
@@ -972,6 +987,9 @@ def main():
         return
     if args.profile:
         profile_steps()
+        return
+    if args.profile_config2:
+        profile_config2(args.profile_config2)
         return
     if args.profile_gemm:
         profile_gemm(args.profile_gemm)

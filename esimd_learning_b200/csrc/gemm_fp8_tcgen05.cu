@@ -28,6 +28,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <type_traits>
 #include <mutex>
@@ -360,6 +361,242 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
 
 // ---- host side ---------------------------------------------------------------------
 
+// ---- the same GEMM on CTA pairs (tcgen05 cta_group::2) ----------------------------
+//
+// A cluster of two CTAs (one per SM) computes a 256 x BN tile: each CTA loads
+// its own 128 rows of A and half of the BN rows of B (BN / 2) with plain TMA
+// (no multicast), and the pair's leader (rank 0) issues
+// tcgen05.mma.cta_group::2 (M = 256), which reads A and B from both CTAs'
+// shared memory and accumulates each CTA's 128 rows into that CTA's TMEM.
+// Per SM this halves the B traffic from L2 and the B tile in shared memory
+// for the same tile width.
+//  * full barriers live in the leader: the leader's producer expects both
+//    CTAs' bytes; the peer's loads complete their bytes on the leader's
+//    barrier (the cta_group::2 form of the TMA load);
+//  * the leader's commits arrive on both CTAs' empty and accumulator-full
+//    barriers (commit with .multicast::cluster);
+//  * both CTAs' epilogue warps arrive on the leader's accumulator-empty
+//    barrier (the peer remotely, through mapa);
+//  * TMEM is allocated and freed by warp 1 of each CTA (cta_group::2), and a
+//    cluster barrier precedes the free, so no MMA is still writing.
+namespace pair {
+
+CEK_DEVICE uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+CEK_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same variable in CTA `rank` of the cluster
+CEK_DEVICE uint32_t map_to(uint32_t saddr_local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr_local), "r"(rank));
+  return r;
+}
+// bounded wait with cluster-scope acquire (the barrier receives arrivals
+// from the peer CTA)
+CEK_DEVICE bool wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kWaitPolls; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    if (ok) return true;
+    if ((i & 1023u) == 1023u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  atomicAdd(&g_timeouts, 1ull);
+  return false;
+}
+CEK_DEVICE void arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+CEK_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(leader_bar) : "memory");
+}
+CEK_DEVICE void mma_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p; }"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
+}
+// arrive on the barrier at this address in both CTAs of the pair
+CEK_DEVICE void commit_both(uint32_t bar) {
+  asm volatile(
+      "{ .reg .b16 m; mov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m; }"
+      ::"r"(bar) : "memory");
+}
+CEK_DEVICE void commit_local(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+template <int BN>
+struct PairTile {
+  static constexpr int A_BYTES = BM * BK, B_BYTES = (BN / 2) * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int THREADS = 6 * 32;
+  static constexpr int STAGES = (kSmemBudget - 2048) / STAGE_BYTES > 8 ? 8 : (kSmemBudget - 2048) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  // e4m3 x e4m3, fp32 accumulate, K-major, N = BN, M = 256 (the pair)
+  static constexpr uint32_t IDESC = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(256 >> 4) << 24);
+};
+
+template <typename OutT, int BN>
+__global__ void __launch_bounds__(PairTile<BN>::THREADS, 1)
+gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const Params p) {
+  using TL = PairTile<BN>;
+  constexpr int STAGES = TL::STAGES, STAGE_BYTES = TL::STAGE_BYTES, A_BYTES = TL::A_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (saddr(smem_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cta_rank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int num_m2 = (p.M + 2 * BM - 1) / (2 * BM);
+  const int num_tiles = num_m2 * p.num_n;
+  const int kblocks = p.kblocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      bar_init(saddr(&full_bar[s]), 1);
+      bar_init(saddr(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(saddr(&acc_full[b]), 1);
+      bar_init(saddr(&acc_empty[b]), 8);  // both CTAs' four epilogue warps (used in the leader)
+    }
+    bar_init(saddr(&drain_bar), 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(&tmem_base_sh)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  fence_before();
+  cluster_sync();
+  fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      pdl_wait();
+      int it = 0;
+      for (int t = cluster; t < num_tiles && !abort_flag; t += nclusters) {
+        const int mb = t % num_m2, nb = t / num_m2;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait(saddr(&empty_bar[s]), ((it / STAGES) & 1) ^ 1, &abort_flag)) break;
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          const uint32_t fb = map_to(saddr(&full_bar[s]), 0);
+          if (leader) bar_expect_tx(saddr(&full_bar[s]), 2 * STAGE_BYTES);
+          tma_load_2d_pair(saddr(sa), &map_a, kb * p.kblock_elems, mb * 2 * BM + (int)rank * BM, fb);
+          tma_load_2d_pair(saddr(sa + A_BYTES), &map_b, kb * p.kblock_elems, nb * BN + (int)rank * (BN / 2), fb);
+        }
+      }
+      // before leaving: our copies have landed once the MMAs that read the
+      // last stages committed (their empty barriers; bounded)
+      for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+        wait(saddr(&empty_bar[j % STAGES]), (j / STAGES) & 1, &abort_flag);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (lane == 0 && leader) {
+      int it = 0, local = 0;
+      for (int t = cluster; t < num_tiles && !abort_flag; t += nclusters, ++local) {
+        const int b = local & 1;
+        if (!wait_cluster(saddr(&acc_empty[b]), ((local >> 1) & 1) ^ 1, &abort_flag)) break;
+        fence_after();
+        const uint32_t d = tmem_base + b * 256;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait_cluster(saddr(&full_bar[s]), (it / STAGES) & 1, &abort_flag)) { ok = false; break; }
+          fence_after();
+          const uint32_t a0 = saddr(smem + s * STAGE_BYTES), b0 = a0 + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k)
+            mma_pair(d, smem_desc(a0 + k * 32), smem_desc(b0 + k * 32), TL::IDESC, (kb | k) ? 1u : 0u);
+          commit_both(saddr(&empty_bar[s]));
+        }
+        if (!ok) break;
+        commit_both(saddr(&acc_full[b]));
+      }
+      commit_local(saddr(&drain_bar));
+      wait(saddr(&drain_bar), 0, &abort_flag);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    pdl_wait();
+    const int quad = warp & 3;
+    OutT* y = static_cast<OutT*>(p.y);
+    const uint32_t leader_empty[2] = {map_to(saddr(&acc_empty[0]), 0), map_to(saddr(&acc_empty[1]), 0)};
+    int local = 0;
+    for (int t = cluster; t < num_tiles && !abort_flag; t += nclusters, ++local) {
+      const int b = local & 1;
+      const int mb = t % num_m2, nb = t / num_m2;
+      if (!wait(saddr(&acc_full[b]), (local >> 1) & 1, &abort_flag)) break;
+      fence_after();
+      const int row = mb * 2 * BM + (int)rank * BM + quad * 32 + lane;
+      const bool rv = row < p.M;
+      const float as = rv ? p.a_scale[row] : 0.f;
+      OutT* yrow = y + (size_t)(rv ? row : 0) * p.N;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + b * 256;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        const int n0 = nb * BN + c;
+        if (rv && n0 < p.N) {
+          const bool hi = n0 + 16 < p.N;
+          uint32_t o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = n0 + 2 * i;
+            const bool nv = i < 8 || hi;
+            const float bs0 = nv ? __ldg(p.b_scale + n) : 0.f;
+            const float bs1 = nv ? __ldg(p.b_scale + n + 1) : 0.f;
+            o[i] = pack2<OutT>(__uint_as_float(r[2 * i]) * as * bs0, __uint_as_float(r[2 * i + 1]) * as * bs1);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(yrow + n0);
+          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          if (hi) {
+            dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+            dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) arrive_remote(leader_empty[b]);
+    }
+  }
+
+  fence_before();
+  __syncwarp();
+  cluster_sync();
+  fence_after();
+  __syncwarp();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+}
+
+}  // namespace pair
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -409,6 +646,93 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaSt
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, ma, mb, p) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
+}
+
+template <typename OutT, int BN>
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t st) {
+  auto kern = pair::gemm_fp8_pair_kernel<OutT, BN>;
+  constexpr int SMEM_BYTES = pair::PairTile<BN>::SMEM_BYTES;
+  static cek_host::DeviceSlots attr_set;
+  const int sms = cek_host::sm_count();
+  if (!cek_host::ensure_smem_attr(attr_set, kern, SMEM_BYTES)) return CEK_ERR_LAUNCH;
+  const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * p.num_n;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)sms);
+  cfg.blockDim = dim3(pair::PairTile<BN>::THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  // as many pairs as can be resident at once (SM pairs within a GPC), once per device
+  static cek_host::DeviceSlots max_pairs;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::atomic<int>* slot = max_pairs.at(dev);
+  int mp = slot ? slot->load() : 0;
+  if (mp <= 0) {
+    cfg.gridDim = dim3((unsigned)sms);
+    if (cudaOccupancyMaxActiveClusters(&mp, kern, &cfg) != cudaSuccess || mp <= 0) mp = sms / 2;
+    if (slot) slot->store(mp);
+  }
+  const int pairs = std::min(tiles, std::min(mp, sms / 2));
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, p) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
+}
+
+// CTA-pair path: CEK_GEMM_PAIR=1 turns it on (per-token FP8 GEMM, M > 128).
+// Off by default: at N = 14336, K = 4096 it measured 106.9 / 365.0 us at
+// M = 2048 / 8192 against 102.4 / 353.3 us for the one-CTA kernel (tensor
+// pipe 55.5 % against 59.9 % of elapsed; L2 at 37-42 % of its peak, so the
+// halved B traffic buys nothing here).
+bool use_pair(int64_t M) {
+  static const int mode = [] {
+    const char* v = std::getenv("CEK_GEMM_PAIR");
+    return v ? std::atoi(v) : 0;
+  }();
+  return mode == 1 && M > BM;
+}
+
+// Tile N for the pair path: as choose_bn over 256-row tiles and SM pairs.
+int choose_bn_pair(int64_t M, int64_t N) {
+  const int pairs = cek_host::sm_count() / 2;  // (the resident pairs are at most this)
+  const int64_t num_m2 = (M + 2 * BM - 1) / (2 * BM);
+  const int cands[4] = {256, 224, 192, 160};
+  int bn = 256;
+  int64_t best = INT64_MAX / 100;
+  for (int c : cands) {
+    const int64_t tiles = num_m2 * ((N + c - 1) / c);
+    const int64_t cost = ((tiles + pairs - 1) / pairs) * c;
+    if (cost * 100 < best * 97) { best = cost; bn = c; }
+  }
+  return bn;
+}
+
+int run_pair(const void* a, const void* b, const float* a_scale, const float* b_scale, void* y, int64_t M,
+             int64_t N, int64_t K, int y_dtype, cudaStream_t st) {
+  const int bn = choose_bn_pair(M, N);
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a, M, K, BM) || !make_map(&mb, b, N, K, bn / 2)) return CEK_ERR_LAUNCH;
+  Params p;
+  p.a_scale = a_scale; p.b_scale = b_scale; p.y = y;
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.num_m = (int)((M + BM - 1) / BM);
+  p.num_n = (int)((N + bn - 1) / bn);
+  p.kblocks = (int)(K / BK);
+  p.kblock_elems = BK;
+  p.b_scalar = 0;
+#define CEK_GEMM_PAIR_BN(B)                                                               \
+  if (bn == B) return y_dtype == CEK_F16 ? launch_pair<__half, B>(ma, mb, p, st)         \
+                                         : launch_pair<__nv_bfloat16, B>(ma, mb, p, st);
+  CEK_GEMM_PAIR_BN(256) CEK_GEMM_PAIR_BN(224) CEK_GEMM_PAIR_BN(192) CEK_GEMM_PAIR_BN(160)
+#undef CEK_GEMM_PAIR_BN
+  return CEK_ERR_UNSUPPORTED;
 }
 
 int choose_bn(int64_t M, int64_t N) {
@@ -498,6 +822,7 @@ extern "C" int cek_gemm_fp8_scaled(const void* aq, const void* bq, const float* 
   if (!cek_host::aligned16(aq) || !cek_host::aligned16(bq) || !cek_host::aligned16(y))
     return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cek::gemm::use_pair(M)) return cek::gemm::run_pair(aq, bq, a_scale, b_scale, y, M, N, K, y_dtype, st);
   return cek::gemm::run<cek::gemm::kE4M3>(aq, bq, a_scale, b_scale, false, y, M, N, K, 1, y_dtype, st);
 }
 

@@ -10,6 +10,8 @@
   shapes and ragged M / N edges, against the fp32 oracle of the same
   quantised operands; quantisation itself is bit-exact (test_elementwise).
 """
+from pathlib import Path
+
 import pytest
 import torch
 
@@ -194,3 +196,37 @@ def test_tcgen05_gemm_rejects_bad_shapes(cuda_device):
     L = cabi.lib()
     assert L.cek_gemm_fp8_scaled(16, 16, 16, 16, 16, 128, 256, 100, 0, None) == cabi.CEK_ERR_INVALID_ARG
     assert L.cek_gemm_fp8_scaled(16, 16, 16, 16, 16, 128, 250, 128, 0, None) == cabi.CEK_ERR_INVALID_ARG
+
+
+def test_tcgen05_gemm_cta_pair_path(cuda_device):
+    """The CTA-pair variant of the per-token FP8 GEMM (tcgen05 cta_group::2,
+    cluster of 2, enabled by CEK_GEMM_PAIR=1) against the oracle, in a child
+    process (the switch is read once per process): ragged M and N edges, and
+    the config-3 shape."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import sys, ctypes, torch
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[1] + "/python")
+import esimd_learning_b200 as ops
+from esimd_learning_b200 import cabi
+from esimd_learning_b200.workloads import prefill_case
+from oracle import oracle as O
+dev = torch.device("cuda", 0)
+for M, N, K in [(256, 512, 256), (300, 1040, 512), (1000, 2048, 1024), (2048, 14336, 4096)]:
+    a, bq, bs = prefill_case(M, N=N, K=K, seed=M)
+    aq, as_ = O.quant_fp8_per_token(a)
+    y = torch.full((M, N), float("nan"), dtype=torch.float16, device=dev)
+    ops.esimd_gemm_fp8_pertoken_pern(aq.to(dev), as_.to(dev), bq.to(dev), bs.to(dev), y)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y).all(), (M, N, K)
+    rows = torch.arange(0, M, max(1, M // 61))
+    O.assert_parity(y.cpu()[rows], O.gemm_fp8_scaled(aq[rows], as_[rows], bq, bs), f"pair M={M} N={N} K={K}")
+n = ctypes.c_uint64(1); cabi.call("cek_gemm_fp8_timeouts", ctypes.byref(n)); assert n.value == 0
+print("pair ok")
+'''
+    root = str(Path(__file__).resolve().parent.parent)
+    r = subprocess.run([sys.executable, "-c", code, root], capture_output=True, text=True, timeout=600,
+                       env={**os.environ, "CEK_GEMM_PAIR": "1"})
+    assert r.returncode == 0 and "pair ok" in r.stdout, r.stdout[-2000:] + r.stderr[-3000:]

@@ -491,6 +491,7 @@ def run_ours(args, rank, world, local):
     }
     out["config0"] = measure_config0(dev)
     out["config2"] = measure_config2(dev)
+    out["elementwise"] = measure_elementwise(dev)
     if not args.no_gemm:
         out["gemm"] = {f"M{M}": measure_gemm(dev, M) for M in (2048, 8192)}
     if not args.no_chain:
@@ -745,6 +746,53 @@ def measure_config2(dev, reps_per_copy: int = 4) -> dict:
                         "gbs": round(b / (fused * 1e-6) / 1e9, 1), "frac": round(b / (fused * 1e-6) / 1e9 / peak, 4)}
     del copies
     torch.cuda.empty_cache()
+    return res
+
+
+def measure_elementwise(dev, reps: int = 400) -> dict:
+    """The decode-chain helpers at config-4 shapes (TP = 1): GeLU(tanh)-and-mul
+    on [M, 2 x 28672] and q/k-norm + RoPE on [M, 80 heads x 128] (64 q, 8 k
+    heads normed and rotated), M = 1, 8, 16.  CUDA graph of `reps`
+    back-to-back calls, CUDA events, per-call mean.  The tensors are small
+    enough to stay in L2, so these are launch- and latency-bound; the
+    fraction is reported against the HBM copy peak for reference only."""
+    import esimd_learning_b200 as ops
+    from oracle import oracle as O  # the cos/sin cache builder only
+    st = torch.cuda.Stream(dev)
+    peak, _ = peaks()
+
+    def graph_us(fn):
+        with torch.cuda.stream(st):
+            fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                for _ in range(reps):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            g.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    res = {"timing": "CUDA graph of back-to-back calls (L2-resident inputs)"}
+    d, hq, hkv, D = 28672, 64, 8, 128
+    cs = O.rope_cos_sin_cache(8192, D, 500000.0).to(dev)
+    qw = torch.ones(D, dtype=torch.float16, device=dev)
+    for M in (1, 8, 16):
+        x = torch.randn(M, 2 * d, device=dev).half()
+        o = torch.empty(M, d, device=dev, dtype=torch.float16)
+        us = graph_us(lambda: ops.esimd_gelu_and_mul(x, o))
+        b = 6 * M * d
+        res[f"gelu_and_mul_M{M}"] = {"us": round(us, 3), "bytes": b, "gbs": round(b / (us * 1e-6) / 1e9, 1)}
+        qkv = torch.randn(M, (hq + 2 * hkv) * D, device=dev).half()
+        pos = torch.randint(0, 8192, (M,), device=dev)
+        us = graph_us(lambda: ops.esimd_qkv_norm_rope(qkv, pos, qw, qw, cs, hq, hkv, D, 1e-6, True))
+        b = 2 * 2 * M * (hq + hkv) * D + 4 * M * D
+        res[f"qkv_norm_rope_M{M}"] = {"us": round(us, 3), "bytes": b, "gbs": round(b / (us * 1e-6) / 1e9, 1)}
     return res
 
 

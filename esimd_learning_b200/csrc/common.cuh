@@ -199,6 +199,24 @@ inline bool ensure_smem_attr(DeviceSlots& slots, Kern kern, int bytes) {
   if (c) c->store(bytes, std::memory_order_relaxed);
   return true;
 }
+// Launch with programmatic stream serialization (unless CEK_DISABLE_PDL=1):
+// the kernel may start while the previous kernel on the stream drains; it
+// must execute griddepcontrol.wait before touching anything that kernel
+// writes.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
+}
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;

@@ -17,6 +17,8 @@ namespace cek {
 template <typename T>
 __global__ void __launch_bounds__(256)
 gelu_and_mul_kernel(const T* __restrict__ x, T* __restrict__ out, int d) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int m = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element group index
   if (v * 8 >= d) return;
@@ -47,6 +49,8 @@ __global__ void __launch_bounds__(256)
 qkv_norm_rope_kernel(T* qkv, const int64_t* __restrict__ pos, const T* __restrict__ qw,
                      const T* __restrict__ kw, const float* __restrict__ cos_sin, int M, int hq,
                      int hkv, int max_pos, float eps) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int D = 64 * E;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -108,6 +112,8 @@ __global__ void __launch_bounds__(256)
 quant_fp8_per_token_kernel(const T* __restrict__ a, uint8_t* __restrict__ q, float* __restrict__ sc,
                            int K) {
   __shared__ float sh[8];
+  pdl_launch_dependents();
+  pdl_wait();
   const int m = blockIdx.x;
   const T* row = a + (size_t)m * K;
   const int nvec = K >> 3;
@@ -166,12 +172,8 @@ extern "C" int cek_gelu_and_mul(const void* x, void* out, int64_t M, int64_t d, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dim3 grid((unsigned)(((d + 7) / 8 + 255) / 256), (unsigned)M), block(256);
   if (dtype == CEK_F16)
-    cek::gelu_and_mul_kernel<__half><<<grid, block, 0, st>>>(
-        static_cast<const __half*>(x), static_cast<__half*>(out), (int)d);
-  else
-    cek::gelu_and_mul_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), (int)d);
-  return cek_host::launch_status();
+    return cek_host::launch_pdl(cek::gelu_and_mul_kernel<__half>, grid, block, 0, st, x, out, (int)d);
+  return cek_host::launch_pdl(cek::gelu_and_mul_kernel<__nv_bfloat16>, grid, block, 0, st, x, out, (int)d);
 }
 
 extern "C" int cek_qkv_norm_rope(void* qkv, const int64_t* positions, const void* q_weight,
@@ -189,10 +191,10 @@ extern "C" int cek_qkv_norm_rope(void* qkv, const int64_t* positions, const void
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dim3 grid((unsigned)((warps * 32 + 255) / 256)), block(256);
   const int m = (int)M, hq = (int)num_q_heads, hkv = (int)num_kv_heads, mp = (int)max_position;
+  int s = CEK_OK;
 #define CEK_ROPE(T, E, NX)                                                                       \
-  cek::qkv_norm_rope_kernel<T, E, NX><<<grid, block, 0, st>>>(                                   \
-      static_cast<T*>(qkv), positions, static_cast<const T*>(q_weight),                          \
-      static_cast<const T*>(k_weight), cos_sin_cache, m, hq, hkv, mp, eps)
+  s = cek_host::launch_pdl(cek::qkv_norm_rope_kernel<T, E, NX>, grid, block, 0, st, qkv, positions,  \
+                           q_weight, k_weight, cos_sin_cache, m, hq, hkv, mp, eps)
 #define CEK_ROPE_E(T, NX)                                       \
   if (head_dim == 64) CEK_ROPE(T, 1, NX);                       \
   else if (head_dim == 128) CEK_ROPE(T, 2, NX);                 \
@@ -204,7 +206,7 @@ extern "C" int cek_qkv_norm_rope(void* qkv, const int64_t* positions, const void
   }
 #undef CEK_ROPE_E
 #undef CEK_ROPE
-  return cek_host::launch_status();
+  return s;
 }
 
 extern "C" int cek_quant_fp8_per_token(const void* a, void* aq, float* a_scale, int64_t M,
@@ -216,14 +218,15 @@ extern "C" int cek_quant_fp8_per_token(const void* a, void* aq, float* a_scale, 
   if (!cek_host::aligned16(a) || (reinterpret_cast<uintptr_t>(aq) & 7u)) return CEK_ERR_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int vpt = (int)((K / 8 + 255) / 256);
+  int s = CEK_OK;
 #define CEK_QUANT(T, V)                                                                      \
-  cek::quant_fp8_per_token_kernel<T, V><<<(unsigned)M, 256, 0, st>>>(                       \
-      static_cast<const T*>(a), static_cast<uint8_t*>(aq), a_scale, (int)K)
+  s = cek_host::launch_pdl(cek::quant_fp8_per_token_kernel<T, V>, dim3((unsigned)M), dim3(256), 0, st, a,  \
+                           aq, a_scale, (int)K)
 #define CEK_QUANT_V(T)                                                                       \
   if (vpt <= 1) CEK_QUANT(T, 1); else if (vpt <= 2) CEK_QUANT(T, 2);                         \
   else if (vpt <= 4) CEK_QUANT(T, 4); else CEK_QUANT(T, 8);
   if (dtype == CEK_F16) { CEK_QUANT_V(__half) } else { CEK_QUANT_V(__nv_bfloat16) }
 #undef CEK_QUANT_V
 #undef CEK_QUANT
-  return cek_host::launch_status();
+  return s;
 }

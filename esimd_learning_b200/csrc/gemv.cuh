@@ -30,25 +30,12 @@ struct GemvParams {
   // [N, 2N) (scale likewise); y [M, N] = io(gelu_tanh(io(gate)) * io(up))
   // (bulk kernel only)
   int y_gelu;
-  // 1: residual add + RMSNorm prologue inside the bulk GEMV.  x is the
-  // hidden state, residual the OLD residual (only read here), gamma the
-  // pre-shifted norm weight; every CTA forms io(f32(io(h + r)) * inv_rms *
-  // gamma) on chip (shared or tensor memory), inv_rms from the unrounded
-  // h + r.  The CTAs trigger their dependents only after their last read of
-  // the residual, so a kernel launched behind them may update it in place.
-  int norm;
-  float eps;
   // tensor-parallel all-reduce epilogue (ar_world > 0, tp_allreduce.cu):
   // y is pushed into slot ar_rank of every rank's receive buffer instead of
   // being stored to p.y.
   const unsigned long long* ar_peers;  // device array [ar_world] of comm base addresses
   unsigned* ar_sync;                   // this rank's sync block
   int ar_rank, ar_world;
-  // column-parallel all-gather epilogue (ag_n > 0, with ar_world ranks):
-  // this call computes rows [ag_row0, ag_row0 + N) of y [M, ag_n] and stores
-  // them at byte offset ag_off of the data area of every rank's comm region.
-  long long ag_off;
-  int ag_n, ag_row0;
   // several weight matrices sharing x in one launch (nmat > 0): matrix m
   // owns CTAs [mcta_off[m], mcta_off[m+1]) and writes ys[m] [M, ns[m]]
   int nmat;
@@ -57,6 +44,19 @@ struct GemvParams {
   void* mys[kMaxMats];
   int mns[kMaxMats];
   int mcta_off[kMaxMats + 1];
+  // column-parallel all-gather epilogue (ag_n > 0, with ar_world ranks):
+  // this call computes rows [ag_row0, ag_row0 + N) of y [M, ag_n] and stores
+  // them at byte offset ag_off of the data area of every rank's comm region.
+  long long ag_off;
+  int ag_n, ag_row0;
+  // 1: residual add + RMSNorm prologue inside the bulk GEMV.  x is the
+  // hidden state, residual the OLD residual (only read here), gamma the
+  // pre-shifted norm weight; every CTA forms io(f32(io(h + r)) * inv_rms *
+  // gamma) on chip (shared or tensor memory), inv_rms from the unrounded
+  // h + r.  The CTAs trigger their dependents only after their last read of
+  // the residual, so a kernel launched behind them may update it in place.
+  int norm;
+  float eps;
 };
 
 // Layout of a rank's tensor-parallel comm region: a 4 KiB sync block
@@ -86,6 +86,22 @@ CEK_DEVICE unsigned ld_acquire_sys(const unsigned* addr) {
 // local store, the all-reduce push (slot ar_rank of every rank's receive
 // buffer, slot set by the call's epoch parity), or the all-gather push (row
 // ag_row0 + n of every rank's full output).
+// The two push modes, kept out of line and given the fields by value: the
+// kernels' common path is the local store, and inlining the pushes (or
+// letting the parameter block's address escape) slowed the split-K kernel.
+template <typename OutT>
+__device__ __noinline__ void store_out_push(const unsigned long long* peers, const unsigned* sync, int rank, int world,
+                                            long long ag_off, int ag_n, int ag_row0, int M, int N, int tok, int n,
+                                            OutT v) {
+  if (ag_n > 0) {
+    const size_t off = (size_t)tok * ag_n + ag_row0 + n;
+    for (int r = 0; r < world; ++r) reinterpret_cast<OutT*>(peers[r] + tp::kSyncBytes + ag_off)[off] = v;
+  } else {
+    const unsigned set = (*reinterpret_cast<const volatile unsigned*>(&sync[tp::kEpoch]) + 1) & 1u;
+    const size_t off = (((size_t)set * world + rank) * M + tok) * N + n;
+    for (int r = 0; r < world; ++r) reinterpret_cast<OutT*>(peers[r] + tp::kSyncBytes)[off] = v;
+  }
+}
 template <typename OutT>
 CEK_DEVICE void store_out(const GemvParams& p, OutT* y, int ldy, int tok, int n, OutT v) {
   if (p.ar_world == 0) {

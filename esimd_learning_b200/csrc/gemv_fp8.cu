@@ -131,23 +131,31 @@ CEK_DEVICE void consume(const Batch<NT>& b, float (&acc)[NT][4]) {
   }
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT, int NT, bool FUSED>
+// PUSH: the tensor-parallel push epilogues (all-reduce slots or all-gather
+// rows over peer memory) instead of the local store; a separate
+// instantiation, so the plain kernel carries no trace of them.
+template <typename InT, int FMT, int SCALE, typename OutT, int NT, bool FUSED, bool PUSH = false>
 __global__ void __launch_bounds__(kMaxWarps * 32)
-gemv_fp8_kernel(const GemvParams pin) {
+gemv_fp8_kernel(const __grid_constant__ GemvParams p) {
   constexpr int U = Batch<NT>::U;
   __shared__ float red[kMaxWarps][16][NT * 8];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  GemvParams p = pin;
+  // The parameters stay in parameter space (no per-thread copy); a
+  // multi-GEMV CTA overrides its matrix's pointers and row count here.
   int cta = blockIdx.x / p.mtiles;
   const int mt = blockIdx.x % p.mtiles;
+  const uint8_t* pw = p.w;
+  const void* pscale = p.scale;
+  void* py = p.y;
+  int pN = p.N;
   if (p.nmat > 0) {  // multi-GEMV: pick this CTA's matrix
     int m = 0;
     while (m + 1 < p.nmat && cta >= p.mcta_off[m + 1]) ++m;
-    p.w = p.mws[m];
-    p.scale = p.mscales[m];
-    p.y = p.mys[m];
-    p.N = p.mns[m];
+    pw = p.mws[m];
+    pscale = p.mscales[m];
+    py = p.mys[m];
+    pN = p.mns[m];
     cta -= p.mcta_off[m];
   }
   const int rg_local = warp / p.ks, kslice = warp % p.ks;
@@ -160,10 +168,10 @@ gemv_fp8_kernel(const GemvParams pin) {
   const int nchunks = (p.K + kChunkK - 1) / kChunkK;
   const int cbeg = kslice * p.cpw;
   c.cend = min(cbeg + p.cpw, nchunks);
-  c.v0 = row0 < p.N;
-  c.v1 = row1 < p.N;
-  c.w0 = p.w + (size_t)(c.v0 ? row0 : 0) * p.K + c.t * 16;
-  c.w1 = p.w + (size_t)(c.v1 ? row1 : 0) * p.K + c.t * 16;
+  c.v0 = row0 < pN;
+  c.v1 = row1 < pN;
+  c.w0 = pw + (size_t)(c.v0 ? row0 : 0) * p.K + c.t * 16;
+  c.w1 = pw + (size_t)(c.v1 ? row1 : 0) * p.K + c.t * 16;
 
   // No early griddepcontrol.launch_dependents here: the kernel that follows
   // is often the persistent bulk GEMV (one 220 KB CTA per SM), whose CTAs,
@@ -213,12 +221,16 @@ gemv_fp8_kernel(const GemvParams pin) {
     const int tl = e / rows_cta, rr = e % rows_cta;
     const int tok = c.tok_base + tl;
     const int n = cta * rows_cta + rr;
-    if (tok >= p.M || n >= p.N) continue;
+    if (tok >= p.M || n >= pN) continue;
     const int rgl = rr >> 4, r = rr & 15;
     float s = 0.f;
     for (int q = 0; q < p.ks; ++q) s += red[rgl * p.ks + q][r][tl];
-    s *= load_scale<SCALE>(p.scale, n);
-    store_out<OutT>(p, reinterpret_cast<OutT*>(p.y), p.N, tok, n, from_f32<OutT>(s));
+    s *= load_scale<SCALE>(pscale, n);
+    if constexpr (!PUSH)
+      reinterpret_cast<OutT*>(py)[(size_t)tok * pN + n] = from_f32<OutT>(s);
+    else
+      store_out_push<OutT>(p.ar_peers, p.ar_sync, p.ar_rank, p.ar_world, p.ag_off, p.ag_n, p.ag_row0, p.M, p.N, tok,
+                           n, from_f32<OutT>(s));
   }
 }
 
@@ -273,7 +285,8 @@ static int launch_one(const GemvParams& p, const GemvLaunch& L, cudaStream_t st)
   attr[0].val.programmaticStreamSerializationAllowed = (cek_host::pdl_enabled() && FUSED) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_fp8_kernel<InT, FMT, SCALE, OutT, NT, FUSED>, p);
+  cudaError_t e = p.ar_world > 0 ? cudaLaunchKernelEx(&cfg, gemv_fp8_kernel<InT, FMT, SCALE, OutT, NT, FUSED, true>, p)
+                                  : cudaLaunchKernelEx(&cfg, gemv_fp8_kernel<InT, FMT, SCALE, OutT, NT, FUSED, false>, p);
   return e == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
 }
 

@@ -114,7 +114,7 @@ CEK_API int cek_fused_add_rmsnorm(void* hidden, void* residual, const void* weig
  * xn       = io(f32(residual) * inv_rms[m] * weight)
  * y        = GEMV(xn, w, scale)  as cek_gemv_fp8.
  * Where x [M, K] fits in the bulk GEMV's shared memory beside its weight
- * ring (M <= 2 at K = 4096, M = 1 at K = 8192; e4m3 weights, K % 64 == 0)
+ * ring and K <= 4096 (M <= 2 at K = 4096; e4m3 weights, K % 64 == 0)
  * the GEMV itself forms xn on chip: every CTA reads hidden and residual,
  * reduces the inverse RMS and stages xn, then a small kernel launched
  * behind it (once all CTAs have read the residual) writes the residual.

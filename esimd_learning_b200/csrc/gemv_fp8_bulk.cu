@@ -69,6 +69,15 @@ constexpr int kUnroll = 2;                 // chunk loop unroll when x is in sha
 // used when x does not fit in shared memory beside two slabs).
 constexpr int kXSmem = 0, kXL2 = 1, kXTmem = 2;
 constexpr int kTmemCols = 512;             // all of TMEM: 256 columns per consumer warp
+// Two CTAs per SM (CO = 1, the default for up to 8 tokens): half the shared
+// memory (113 KB a CTA, static part included), half of TMEM and <= 96
+// registers a thread, and a grid of two CTAs per SM, each streaming half of
+// the SM's rows.  The SM keeps as many bytes in flight as one big CTA did,
+// and when one CTA exits the next launch's CTA takes its place (prefetching
+// its first slabs) while the other still drains, so consecutive launches
+// overlap at their boundary.  Config-1 step (12 launches): 205.7 -> 179.9 us.
+constexpr int kCoSmemPerCta = 113 * 1024;
+__host__ __device__ constexpr int tmem_cols(int co) { return co ? kTmemCols / 2 : kTmemCols; }
 
 __device__ unsigned long long g_timeouts;
 #ifdef CEK_BULK_TRACE
@@ -82,7 +91,7 @@ CEK_DEVICE unsigned long long gtime() { unsigned long long t; asm volatile("mov.
 
 // x_bytes: x staged in shared memory; ks: bytes of a row per slab (K / pieces);
 // slab_bytes = 16 * ks.
-struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid, xmode, nt; };
+struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid, xmode, nt, co; };
 
 // Row blocks over the rows of one matrix, or of up to kMaxMats matrices
 // sharing x (multi-GEMV, rows concatenated): a block is at most `bsz` rows
@@ -125,8 +134,8 @@ CEK_DEVICE int count_blocks(const GemvParams& p, int r0, int r1, int bsz) {
 
 // NT: 8-token groups (the n8 columns of the MMA), 1 for M <= 8, 2 for M <= 16.
 // NORM: the residual add + RMSNorm prologue (GemvParams::norm).
-template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM, int CO = 0>
+__global__ void __launch_bounds__(kThreads, CO ? 2 : 1)
 gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], xbar;
@@ -355,13 +364,13 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   if constexpr (XM == kXTmem) {
     if (cw == 0) {
       asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                   ::"r"(mbar::saddr(&tmem_base)), "r"(kTmemCols) : "memory");
+                   ::"r"(mbar::saddr(&tmem_base)), "r"(tmem_cols(CO)) : "memory");
       asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    xt = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (cw >= 4 ? kTmemCols / 2 : 0);
+    xt = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (cw >= 4 ? tmem_cols(CO) / 2 : 0);
     if constexpr (!NORM) {
       for (int j = 0; cw + j * kConsumers < K / 64; ++j) {
 #pragma unroll
@@ -480,7 +489,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
                       xa[1], xb[1]);
         }
       } else if (x_smem) {
-#pragma unroll (kUnroll)
+#pragma unroll (CO ? 1 : kUnroll)
         for (int c = cw; c < nchunks; c += kConsumers) {
           uint4 xa[NT], xb[NT];
 #pragma unroll
@@ -494,7 +503,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       } else {
         // x from L2: a batch of kXBatch / NT chunks issues all its activation
         // loads before the first MMA
-        constexpr int XB = kXBatch / NT;
+        constexpr int XB = kXBatch / NT / (CO ? 2 : 1);
         for (int c0 = cw; c0 < nchunks; c0 += XB * kConsumers) {
           uint4 xa[XB][NT], xb[XB][NT];
 #pragma unroll
@@ -559,7 +568,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (cw == 0)
-      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols(CO)) : "memory");
   }
   // the CTA's shared memory must outlive the x copy into it
   if (XM == kXSmem && !x_smem && cw == 0 && !mbar::wait(mbar::saddr(&xbar), 0, kWaitPolls) && lane == 0)
@@ -575,13 +584,14 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
 constexpr int kMinRowCopy = 3072;
 constexpr int kRowPad = 0;  // shared-memory row padding (16 measured no faster)
 
-static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want, int64_t budget) {
+static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want, int64_t budget,
+                     int64_t min_copy = kMinRowCopy) {
   const int64_t room = budget - x_bytes;
   if (room <= 0) return false;
   for (int64_t P = 1; P <= 16; ++P) {
     if (K % (64 * P) != 0) continue;
     const int64_t ks = K / P;
-    if (P > 1 && ks < kMinRowCopy) break;
+    if (P > 1 && ks < min_copy) break;
     const int64_t pitch = ks + kRowPad;
     const int64_t st = room / (kSlabRows * pitch);
     if (st >= want) {
@@ -597,12 +607,16 @@ static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want, int64_t bud
   return false;
 }
 
-Plan plan(int64_t M, int64_t N, int64_t K) {
+Plan plan(int64_t M, int64_t N, int64_t K, int co = 0, int gridx = 1) {
   Plan pl = {};
   if (M < 1 || M > 16 || K % 64 != 0 || K <= 0 || N <= 0 || K > (1 << 20)) return pl;
   const int nt = M <= 8 ? 1 : 2;
+  if (co && nt != 1) return pl;
   // the static reduction array grows with the token groups (8 KB each)
-  const int64_t budget = kSmemBudget - (nt - 1) * 8 * 1024;
+  const int64_t budget = co ? kCoSmemPerCta - 9 * 1024 : kSmemBudget - (nt - 1) * 8 * 1024;
+  // two CTAs per SM: row pieces of at least 2 KB (16 copies of 1 KB per slab
+  // measured 1.4-2x slower), and no two-slab plan (x from L2 instead)
+  const int64_t mc = co ? 2048 : kMinRowCopy;
   const int64_t xb = ((M * K * 2) + 127) / 128 * 128;
   // x in shared memory with three slabs; else x in tensor memory (when its
   // layout fits) with three slabs; else x in shared memory with two; else x
@@ -611,17 +625,17 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   // columns per warp, 256 available, and chunk ownership (every 8th chunk)
   // must not change across K pieces.
   auto tmem_fits = [&](const Plan& q) {
-    return K % 512 == 0 && nt * K / 64 <= kTmemCols / 2 && (q.ks / 64) % kConsumers == 0;
+    return K % 512 == 0 && nt * K / 64 <= tmem_cols(co) / 2 && (q.ks / 64) % kConsumers == 0;
   };
   Plan t = {};
-  if (try_plan(pl, xb, K, 3, budget)) {
+  if (try_plan(pl, xb, K, 3, budget, mc)) {
     pl.xmode = kXSmem;
-  } else if (try_plan(t, 0, K, 3, budget) && tmem_fits(t)) {
+  } else if (try_plan(t, 0, K, 3, budget, mc) && tmem_fits(t)) {
     pl = t;
     pl.xmode = kXTmem;
-  } else if (try_plan(pl, xb, K, 2, budget)) {
+  } else if (!co && try_plan(pl, xb, K, 2, budget, mc)) {
     pl.xmode = kXSmem;
-  } else if (try_plan(pl, 0, K, 3, budget)) {
+  } else if (try_plan(pl, 0, K, 3, budget, mc)) {
     pl.xmode = kXL2;
   } else {
     return Plan{};
@@ -629,15 +643,17 @@ Plan plan(int64_t M, int64_t N, int64_t K) {
   pl.nt = nt;
   pl.smem = pl.x_bytes + pl.stages * pl.slab_bytes;
   const int sms = cek_host::sm_count();
-  pl.grid = (int)std::min<int64_t>(sms, (N + kSlabRows - 1) / kSlabRows);
+  pl.co = co;
+  pl.grid = (int)std::min<int64_t>((int64_t)sms * (co ? gridx : 1), (N + kSlabRows - 1) / kSlabRows);
   return pl;
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM = false>
+template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM = false, int CO = 0>
 int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
-  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM, NT, NORM>;
+  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM, NT, NORM, CO>;
   static cek_host::DeviceSlots configured_smem;
-  constexpr int kMaxDyn = kSmemBudget - (NT - 1) * 8 * 1024;  // beside the static reduction array
+  // beside the static reduction array
+  constexpr int kMaxDyn = CO ? kCoSmemPerCta - 9 * 1024 : kSmemBudget - (NT - 1) * 8 * 1024;
   if (!cek_host::ensure_smem_attr(configured_smem, kern, kMaxDyn)) return CEK_ERR_LAUNCH;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pl.grid);
@@ -657,6 +673,11 @@ int launch_x(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   // the norm prologue (e4m3 weights only) keeps x in shared or tensor memory
   if constexpr (F == CEK_E4M3)
     if (p.norm) return launch<InT, F, S, OutT, kXSmem, NT, true>(p, pl, st);
+  if constexpr (F == CEK_E4M3 && NT == 1)
+    if (pl.co)
+      return pl.xmode == kXSmem   ? launch<InT, F, S, OutT, kXSmem, NT, false, 1>(p, pl, st)
+             : pl.xmode == kXTmem ? launch<InT, F, S, OutT, kXTmem, NT, false, 1>(p, pl, st)
+                                  : launch<InT, F, S, OutT, kXL2, NT, false, 1>(p, pl, st);
   return pl.xmode == kXSmem   ? launch<InT, F, S, OutT, kXSmem, NT>(p, pl, st)
          : pl.xmode == kXTmem ? launch<InT, F, S, OutT, kXTmem, NT>(p, pl, st)
                               : launch<InT, F, S, OutT, kXL2, NT>(p, pl, st);
@@ -689,7 +710,19 @@ int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, i
     return v && v[0] == '0';
   }();
   if (disabled) return CEK_ERR_UNSUPPORTED;
-  const bulk::Plan pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K);
+  // Two CTAs per SM for up to 8 tokens (e4m3), unless CEK_BULK_CO=0;
+  // CEK_BULK_GRIDX=1 gives one CTA per SM per launch (for measurement).
+  static const int co_mode = [] {
+    const char* v = std::getenv("CEK_BULK_CO");
+    return v ? std::atoi(v) : 1;
+  }();
+  static const int gridx = [] {
+    const char* v = std::getenv("CEK_BULK_GRIDX");
+    return v && std::atoi(v) == 1 ? 1 : 2;
+  }();
+  bulk::Plan pl = {};
+  if (co_mode == 1 && !p.norm && w_fmt == CEK_E4M3) pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K, 1, gridx);
+  if (pl.stages == 0) pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K);
   if (pl.stages == 0 || (p.y_gelu && (p.nmat || p.ar_world))) return CEK_ERR_UNSUPPORTED;
   // the norm prologue needs x on chip and a single plain or gated matrix
   // The norm prologue runs where x fits in shared memory beside the ring (one

@@ -672,7 +672,11 @@ template <typename InT, int F, int S, typename OutT, int NT>
 int launch_x(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   // the norm prologue (e4m3 weights only) keeps x in shared or tensor memory
   if constexpr (F == CEK_E4M3)
-    if (p.norm) return launch<InT, F, S, OutT, kXSmem, NT, true>(p, pl, st);
+    if (p.norm) {
+      if constexpr (NT == 1)
+        if (pl.co) return launch<InT, F, S, OutT, kXSmem, NT, true, 1>(p, pl, st);
+      return launch<InT, F, S, OutT, kXSmem, NT, true>(p, pl, st);
+    }
   if constexpr (F == CEK_E4M3 && NT == 1)
     if (pl.co)
       return pl.xmode == kXSmem   ? launch<InT, F, S, OutT, kXSmem, NT, false, 1>(p, pl, st)
@@ -718,10 +722,13 @@ int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, i
   }();
   static const int gridx = [] {
     const char* v = std::getenv("CEK_BULK_GRIDX");
-    return v && std::atoi(v) == 1 ? 1 : 2;
+    const int g = v ? std::atoi(v) : 2;
+    return g >= 1 && g <= 4 ? g : 2;
   }();
   bulk::Plan pl = {};
-  if (co_mode == 1 && !p.norm && w_fmt == CEK_E4M3) pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K, 1, gridx);
+  if (co_mode == 1 && w_fmt == CEK_E4M3) pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K, 1, gridx);
+  // the norm prologue needs x in shared memory: fall back to one CTA per SM
+  if (p.norm && pl.stages && pl.xmode != bulk::kXSmem) pl = bulk::Plan{};
   if (pl.stages == 0) pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K);
   if (pl.stages == 0 || (p.y_gelu && (p.nmat || p.ar_world))) return CEK_ERR_UNSUPPORTED;
   // the norm prologue needs x on chip and a single plain or gated matrix

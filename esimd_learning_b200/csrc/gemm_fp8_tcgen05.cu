@@ -324,19 +324,18 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
         const int n0 = nb * BN + c;
-        if (rv && n0 < p.N) {
-          // N % 16 == 0: the chunk holds 16 or 32 valid columns
-          const bool hi = n0 + 16 < p.N;
-          uint32_t o[16];
+        // the chunk's 32 column scales: one load per lane, then shuffles
+        // (warp-uniform control: every lane takes part)
+        const float bsv = n0 + lane < p.N ? __ldg(p.b_scale + (p.b_scalar ? 0 : n0 + lane)) : 0.f;
+        // N % 16 == 0: the chunk holds 16 or 32 valid columns
+        const bool hi = n0 + 16 < p.N;
+        uint32_t o[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = n0 + 2 * i;
-            const bool nv = i < 8 || hi;
-            const float bs0 = nv ? __ldg(p.b_scale + (p.b_scalar ? 0 : n)) : 0.f;
-            const float bs1 = nv ? __ldg(p.b_scale + (p.b_scalar ? 0 : n + 1)) : 0.f;
-            o[i] = pack2<OutT>(__uint_as_float(r[2 * i]) * as * bs0,
-                               __uint_as_float(r[2 * i + 1]) * as * bs1);
-          }
+        for (int i = 0; i < 16; ++i) {
+          const float bs0 = __shfl_sync(0xffffffffu, bsv, 2 * i), bs1 = __shfl_sync(0xffffffffu, bsv, 2 * i + 1);
+          o[i] = pack2<OutT>(__uint_as_float(r[2 * i]) * as * bs0, __uint_as_float(r[2 * i + 1]) * as * bs1);
+        }
+        if (rv && n0 < p.N) {
           uint4* dst = reinterpret_cast<uint4*>(yrow + n0);
           dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
           dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
@@ -561,17 +560,15 @@ gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_con
         uint32_t r[32];
         tmem_ld32(taddr + c, r);
         const int n0 = nb * BN + c;
-        if (rv && n0 < p.N) {
-          const bool hi = n0 + 16 < p.N;
-          uint32_t o[16];
+        const float bsv = n0 + lane < p.N ? __ldg(p.b_scale + n0 + lane) : 0.f;
+        const bool hi = n0 + 16 < p.N;
+        uint32_t o[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = n0 + 2 * i;
-            const bool nv = i < 8 || hi;
-            const float bs0 = nv ? __ldg(p.b_scale + n) : 0.f;
-            const float bs1 = nv ? __ldg(p.b_scale + n + 1) : 0.f;
-            o[i] = pack2<OutT>(__uint_as_float(r[2 * i]) * as * bs0, __uint_as_float(r[2 * i + 1]) * as * bs1);
-          }
+        for (int i = 0; i < 16; ++i) {
+          const float bs0 = __shfl_sync(0xffffffffu, bsv, 2 * i), bs1 = __shfl_sync(0xffffffffu, bsv, 2 * i + 1);
+          o[i] = pack2<OutT>(__uint_as_float(r[2 * i]) * as * bs0, __uint_as_float(r[2 * i + 1]) * as * bs1);
+        }
+        if (rv && n0 < p.N) {
           uint4* dst = reinterpret_cast<uint4*>(yrow + n0);
           dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
           dst[1] = make_uint4(o[4], o[5], o[6], o[7]);

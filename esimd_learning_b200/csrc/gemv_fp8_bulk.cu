@@ -726,7 +726,13 @@ int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, i
     return g >= 1 && g <= 4 ? g : 2;
   }();
   bulk::Plan pl = {};
-  if (co_mode == 1 && w_fmt == CEK_E4M3) pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K, 1, gridx);
+  // ... when there are at least as many 16-row blocks as SMs: with fewer,
+  // the grid is not two CTAs per SM anyway and the halved ring only costs
+  // (e.g. one rank's down shard at 4- and 8-way tensor parallelism, 512 or
+  // 1024 rows: 9.5 against 6.1 us)
+  const int64_t nrows = p.y_gelu ? 2 * (int64_t)p.N : p.N;
+  if (co_mode == 1 && w_fmt == CEK_E4M3 && (nrows + 15) / 16 >= cek_host::sm_count())
+    pl = bulk::plan(p.M, nrows, p.K, 1, gridx);
   // the norm prologue needs x in shared memory: fall back to one CTA per SM
   if (p.norm && pl.stages && pl.xmode != bulk::kXSmem) pl = bulk::Plan{};
   if (pl.stages == 0) pl = bulk::plan(p.M, p.y_gelu ? 2 * (int64_t)p.N : p.N, p.K);

@@ -47,6 +47,8 @@ CEK_DEVICE bool wait_at_least(const unsigned* flag, unsigned e, unsigned* errors
 template <typename T>
 __global__ void __launch_bounds__(256)
 tp_reduce_kernel(const unsigned long long* peers, unsigned* sync, T* out, int mn, int rank, int world) {
+  // the next kernel may launch now (it waits for this one before reading out)
+  pdl_launch_dependents();
   pdl_wait();
   const unsigned e = *reinterpret_cast<volatile unsigned*>(&sync[kEpoch]) + 1;
   if (blockIdx.x == 0 && threadIdx.x < world) {
@@ -86,6 +88,7 @@ tp_reduce_kernel(const unsigned long long* peers, unsigned* sync, T* out, int mn
 // by any rank before its own barrier is visible here.
 __global__ void __launch_bounds__(32) tp_barrier_kernel(const unsigned long long* peers, unsigned* sync, int rank,
                                                        int world) {
+  pdl_launch_dependents();
   pdl_wait();
   const unsigned e = *reinterpret_cast<volatile unsigned*>(&sync[kEpoch]) + 1;
   for (int r = threadIdx.x; r < world; r += 32) {

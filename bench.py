@@ -799,7 +799,8 @@ def measure_elementwise(dev, reps: int = 400) -> dict:
 def measure_gemm(dev, M: int, reps: int = 20) -> dict:
     """per-token quantisation of A [M, 4096] fp16 and the
     tcgen05 FP8 GEMM against B [14336, 4096] e4m3 (per-channel scales).  Each
-    timed launch follows an L2 flush (256 MB write); CUDA events on the
+    timed launch follows an L2 flush (256 MB write, then read back so
+    no dirty line is left for the timed launch to write back); CUDA events on the
     launching stream; median over `reps`.  torch._scaled_mm (cuBLASLt FP8,
     row-wise scales) on the same operands is reported beside it."""
     import esimd_learning_b200 as ops
@@ -810,12 +811,17 @@ def measure_gemm(dev, M: int, reps: int = 20) -> dict:
     as_ = torch.empty(M, dtype=torch.float32, device=dev)
     y = torch.empty(M, N, dtype=torch.float16, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_sum = torch.empty((), dtype=torch.int64, device=dev)
     st = torch.cuda.current_stream(dev)
 
     def timed(fn):
         ts = []
         for r in range(reps + 3):
+            # write 256 MB (evicts the operands), then read it back: the read
+            # writes the dirty lines back, so the timed launch starts on a clean
+            # L2 and does not pay for the flush's write-backs
             flush.zero_()
+            torch.sum(flush, dim=0, dtype=torch.int64, out=flush_sum)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
             fn()

@@ -610,8 +610,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Row-major [rows, cols] matrix of `eb`-byte elements; box = box_bytes of a
 // row (one k-block) x box_rows rows (box_rows <= 256, the TMA box limit),
 // 128-byte swizzle unless `dense` (the W8 staging tile).
-bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int eb = 1,
-              int box_bytes = BK, bool dense = false) {
+bool encode_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int eb,
+                int box_bytes, bool dense) {
   auto enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -622,6 +622,49 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
              dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
              dense ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Encoded maps of recent calls, keyed by everything the encoding reads.  A
+// layer calls the GEMM with the same weight (and usually the same activation
+// buffer) every step, so the host-side encode runs once per buffer instead of
+// once per call.  A map holds only the address and the shape; a buffer freed
+// and reallocated at the same address with the same shape encodes identically.
+struct MapKey {
+  const void* base;
+  int64_t rows, cols;
+  int box_rows, eb, box_bytes;
+  bool dense;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && box_rows == o.box_rows && eb == o.eb &&
+           box_bytes == o.box_bytes && dense == o.dense;
+  }
+};
+constexpr int kMapCacheSize = 64;
+struct MapCache {
+  std::mutex mu;
+  MapKey key[kMapCacheSize];
+  CUtensorMap map[kMapCacheSize];
+  int used = 0, next = 0;
+};
+
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int eb = 1,
+              int box_bytes = BK, bool dense = false) {
+  static MapCache cache;
+  const MapKey k{base, rows, cols, box_rows, eb, box_bytes, dense};
+  {
+    std::lock_guard<std::mutex> g(cache.mu);
+    for (int i = 0; i < cache.used; ++i)
+      if (cache.key[i] == k) {
+        *m = cache.map[i];
+        return true;
+      }
+  }
+  if (!encode_map(m, base, rows, cols, box_rows, eb, box_bytes, dense)) return false;
+  std::lock_guard<std::mutex> g(cache.mu);
+  const int slot = cache.used < kMapCacheSize ? cache.used++ : (cache.next++ % kMapCacheSize);
+  cache.key[slot] = k;
+  cache.map[slot] = *m;
+  return true;
 }
 
 template <typename OutT, int BN, int KIND, int WFMT = 0>

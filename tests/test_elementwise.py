@@ -40,7 +40,7 @@ def test_qkv_norm_rope(ext, cuda_device, hq, hkv, D, neox, io):
     O.assert_parity(qc[:, :v0], ref[:, :v0], f"hq={hq} hkv={hkv} D={D} neox={neox}")
 
 
-@pytest.mark.parametrize("M,K", [(1, 4096), (2048, 4096), (5, 8), (33, 1000), (7, 8192), (3, 16384)])
+@pytest.mark.parametrize("M,K", [(1, 4096), (2048, 4096), (13, 4096), (5, 8), (33, 1000), (7, 8192), (3, 16384), (9, 2048)])
 @pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
 def test_quant_fp8_per_token_bit_exact(ext, cuda_device, M, K, io):
     torch.manual_seed(2)
@@ -181,3 +181,42 @@ def test_quant_every_16bit_value_many_scales(ext, cuda_device, io):
     rq, rs = O.quant_fp8_per_token(a)
     assert torch.equal(s.cpu(), rs)
     assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
+
+
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+def test_quant_near_e4m3_ties_many_scales(ext, cuda_device, io):
+    """Values placed on and next to the e4m3 rounding midpoints of a / s,
+    over 4096 rows whose scales span the 16-bit type's whole range (plus a
+    row with an infinite input and one with a NaN): the kernel's quotient must round to the
+    same code as torch's IEEE division, bit for bit, and the scales agree."""
+    g = torch.Generator().manual_seed(11)
+    M, K = 4096, 1024
+    lo, hi = (-20, 15) if io == torch.float16 else (-120, 120)
+    amax = 2.0 ** torch.randint(lo, hi, (M, 1), generator=g).double() * (1 + torch.rand(M, 1, generator=g, dtype=torch.float64))
+    s = (amax.float() / 448.0).double()
+    # e4m3 codes 0..447 and the midpoints between neighbouring codes
+    codes = torch.arange(0, 256, dtype=torch.uint8).view(torch.float8_e4m3fn).double()
+    codes = codes[torch.isfinite(codes) & (codes >= 0)].sort().values
+    mids = (codes[1:] + codes[:-1]) / 2
+    pick = torch.randint(0, mids.numel(), (M, K), generator=g)
+    sign = torch.where(torch.rand(M, K, generator=g) < 0.5, -1.0, 1.0).double()
+    a = (mids[pick] * sign * s).to(io)
+    # nudge a third of them one 16-bit step either way
+    bits = a.view(torch.int16)
+    nudge = torch.randint(-1, 2, (M, K), generator=g).to(torch.int16)
+    a = (bits + nudge).view(io)
+    a[:, 0] = amax.squeeze(1).to(io)
+    a = torch.where(torch.isfinite(a.float()), a, torch.zeros_like(a))
+    a[M - 1, 5] = float("inf")
+    a[M - 2, 9] = float("nan")  # torch's amax propagates NaN: scale and codes NaN
+    q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=cuda_device)
+    sc = torch.empty(M, dtype=torch.float32, device=cuda_device)
+    ext.esimd_quant_fp8_per_token(a.to(cuda_device), q, sc)
+    rq, rs = O.quant_fp8_per_token(a)
+    assert torch.isnan(rs[M - 2]) and torch.isinf(rs[M - 1])
+    assert torch.allclose(sc.cpu(), rs, rtol=0, atol=0, equal_nan=True)
+    got, want = q.cpu().view(torch.uint8), rq.view(torch.uint8)
+    # inf / inf is NaN on both sides; its sign bit is the platform's default NaN
+    nan = (want & 0x7F) == 0x7F
+    assert torch.equal((got & 0x7F)[nan], want[nan] & 0x7F)
+    assert torch.equal(got[~nan], want[~nan])

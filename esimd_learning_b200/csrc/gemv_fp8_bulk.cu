@@ -91,7 +91,51 @@ CEK_DEVICE unsigned long long gtime() { unsigned long long t; asm volatile("mov.
 
 // x_bytes: x staged in shared memory; ks: bytes of a row per slab (K / pieces);
 // slab_bytes = 16 * ks.
-struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid, xmode, nt, co; };
+// cl: CTAs per cluster splitting each row block along K (0 = no split).
+struct Plan { int x_bytes, ks, pieces, pitch, slab_bytes, stages, smem, grid, xmode, nt, co, cl; };
+
+// ---- K split over a thread-block cluster -------------------------------------
+// For shapes with fewer 16-row blocks than SMs (a tensor-parallel shard of a
+// short weight: 512 rows x 14336 at 8-way), the row blocks alone would leave
+// most SMs idle.  Then a cluster of C CTAs shares one row block: CTA r of the
+// cluster streams the K slice [r K / C, (r + 1) K / C) of its 16 rows (and
+// the same slice of x), and the non-leader CTAs write their partial row sums
+// into the leader's shared memory (distributed shared memory, st.shared::
+// cluster) and arrive on the leader's mbarrier (release at cluster scope);
+// the leader waits for them (bounded, acquire at cluster scope), adds the
+// partial sums in rank order (deterministic) and runs the epilogue.  No
+// global scratch.  Every CTA ends with a cluster barrier, so no CTA exits
+// while another may still write into its shared memory.
+CEK_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+CEK_DEVICE void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+CEK_DEVICE uint32_t map_leader(uint32_t saddr_local) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(saddr_local));
+  return r;
+}
+CEK_DEVICE void st_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+CEK_DEVICE void arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+CEK_DEVICE bool wait_cluster(uint32_t bar, uint32_t parity, uint32_t polls) {
+  for (uint32_t i = 0; i < polls; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+constexpr int kMaxCluster = 8;
 
 // Row blocks over the rows of one matrix, or of up to kMaxMats matrices
 // sharing x (multi-GEMV, rows concatenated): a block is at most `bsz` rows
@@ -134,7 +178,8 @@ CEK_DEVICE int count_blocks(const GemvParams& p, int r0, int r1, int bsz) {
 
 // NT: 8-token groups (the n8 columns of the MMA), 1 for M <= 8, 2 for M <= 16.
 // NORM: the residual add + RMSNorm prologue (GemvParams::norm).
-template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM, int CO = 0>
+// CL: K split over a cluster of pl.cl CTAs (one 16-row block per cluster).
+template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM, int CO = 0, bool CL = false>
 __global__ void __launch_bounds__(kThreads, CO ? 2 : 1)
 gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -145,8 +190,14 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = p.K, KS = pl.ks, P = pl.pieces;
   const int nrows = total_rows(p);
-  const int r0 = (int)((int64_t)nrows * blockIdx.x / gridDim.x);
-  const int r1 = (int)((int64_t)nrows * (blockIdx.x + 1) / gridDim.x);
+  // K split: this CTA's slice [koff, koff + KC) of every row and of x
+  const int crank = CL ? (int)cluster_rank() : 0;
+  const int KC = CL ? K / pl.cl : K, koff = crank * KC;
+  const int r0 = CL ? (int)(blockIdx.x / pl.cl) * kSlabRows
+                    : (int)((int64_t)nrows * blockIdx.x / gridDim.x);
+  const int r1 = CL ? min(nrows, r0 + kSlabRows) : (int)((int64_t)nrows * (blockIdx.x + 1) / gridDim.x);
+  __shared__ float cred[CL ? kMaxCluster : 1][CL ? kSlabRows : 1][CL ? 8 : 1];  // partial sums (leader)
+  __shared__ __align__(8) uint64_t credbar;
   // gated GeLU output: a block is 8 gate rows (slab rows 0-7) and the
   // matching 8 up rows N + j (slab rows 8-15); rows count row pairs
   const int bsz = p.y_gelu ? kSlabRows / 2 : kSlabRows;
@@ -160,9 +211,14 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
       mbar::init(mbar::saddr(&empty[s]), kConsumers);
     }
     mbar::init(mbar::saddr(&xbar), 1);
+    // the leader's reduction barrier: one arrival per epilogue thread of
+    // every other CTA of the cluster
+    if (CL) mbar::init(mbar::saddr(&credbar), (uint32_t)(pl.cl - 1) * kSlabRows * 8);
     mbar::fence_init();
   }
   __syncthreads();
+  // the leader's barrier is initialised before any CTA of the cluster arrives
+  if constexpr (CL) cluster_sync_all();
   if constexpr (!NORM) pdl_launch_dependents();
 #ifdef CEK_BULK_TRACE
   __shared__ unsigned trace_slot;
@@ -189,12 +245,12 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     auto issue = [&](int i) {
       const int s = i % stages, pc = i % P;
       if (pc == 0) cur.next(p, bm, brow, rows);
-      const uint8_t* wm = (p.nmat ? p.mws[bm] : p.w) + (size_t)brow * K;
+      const uint8_t* wm = (p.nmat ? p.mws[bm] : p.w) + (size_t)brow * K + koff;
       const uint32_t dst = ring + (uint32_t)s * pl.slab_bytes;
       const uint32_t bar = mbar::saddr(&full[s]);
       if (lane == 0) mbar::arrive_expect_tx(bar, (p.y_gelu ? 2u : 1u) * (uint32_t)rows * (uint32_t)KS);
       __syncwarp();
-      if (P == 1 && pl.pitch == KS) {
+      if (!CL && P == 1 && pl.pitch == KS) {
         if (lane == 0) {
           const uint32_t bytes = (uint32_t)rows * (uint32_t)K;
           for (uint32_t off = 0; off < bytes; off += kPiece)
@@ -221,10 +277,20 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     if (XM == kXSmem && lane == 0 && !NORM) {
       const uint32_t xb = (uint32_t)p.M * (uint32_t)K * 2u;
       const uint32_t bar = mbar::saddr(&xbar);
-      mbar::arrive_expect_tx(bar, xb);
       const uint8_t* xs = static_cast<const uint8_t*>(p.x);
-      for (uint32_t off = 0; off < xb; off += kPiece)
-        mbar::bulk_g2s(mbar::saddr(smem) + off, xs + off, min(kPiece, xb - off), bar);
+      if constexpr (CL) {
+        // this CTA's K slice of every token's row, packed with row length KC
+        const uint32_t rb = (uint32_t)KC * 2u;
+        mbar::arrive_expect_tx(bar, (uint32_t)p.M * rb);
+        for (int m = 0; m < p.M; ++m)
+          for (uint32_t off = 0; off < rb; off += kPiece)
+            mbar::bulk_g2s(mbar::saddr(smem) + (uint32_t)m * rb + off, xs + ((size_t)m * K + koff) * 2u + off,
+                           min(kPiece, rb - off), bar);
+      } else {
+        mbar::arrive_expect_tx(bar, xb);
+        for (uint32_t off = 0; off < xb; off += kPiece)
+          mbar::bulk_g2s(mbar::saddr(smem) + off, xs + off, min(kPiece, xb - off), bar);
+      }
     }
     if (!p.early_weights)
       for (int i = 0; i < pre; ++i) issue(i);
@@ -251,6 +317,7 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
           atomicAdd(&g_timeouts, 1ull);
           break;
         }
+    if constexpr (CL) cluster_sync_all();
     return;
   }
 
@@ -264,8 +331,8 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
 #pragma unroll
   for (int u = 0; u < NT; ++u) {
     const int xtok = g + 8 * u < p.M ? g + 8 * u : 0;
-    xrow[u] = mbar::saddr(smem) + (uint32_t)xtok * K * 2u + 32u * t;
-    xglob[u] = reinterpret_cast<const InT*>(p.x) + (size_t)xtok * K + 16 * t;
+    xrow[u] = mbar::saddr(smem) + (uint32_t)xtok * KC * 2u + 32u * t;
+    xglob[u] = reinterpret_cast<const InT*>(p.x) + (size_t)xtok * K + koff + 16 * t;
   }
   const int nchunks = KS / 64;
   bool dead = false;
@@ -544,6 +611,22 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     if (ctid < bsz * 8 * NT) {
       const int tok = ctid / bsz, row = ctid % bsz;
+      if constexpr (CL) {
+        // K split: the other CTAs hand their partial sums to the leader
+        float v = 0.f;
+#pragma unroll
+        for (int q = 0; q < kConsumers; ++q) v += rd[q][row][tok];
+        if (crank != 0) {
+          st_cluster_f32(map_leader(mbar::saddr(&cred[crank][row][tok])), v);
+          arrive_remote(map_leader(mbar::saddr(&credbar)));
+          continue;
+        }
+        if (!wait_cluster(mbar::saddr(&credbar), 0, kWaitPolls)) atomicAdd(&g_timeouts, 1ull);
+        for (int r = 1; r < pl.cl; ++r) v += cred[r][row][tok];
+        if (tok < p.M && out_ok)
+          store_out<OutT>(p, reinterpret_cast<OutT*>(p.y), p.N, tok, out_row, from_f32<OutT>(v * out_scale));
+        continue;
+      }
       if (tok < p.M && out_ok) {
         float v = 0.f;
 #pragma unroll
@@ -574,6 +657,9 @@ gemv_bulk_kernel(const GemvParams p, const Plan pl) {
   if (XM == kXSmem && !x_smem && cw == 0 && !mbar::wait(mbar::saddr(&xbar), 0, kWaitPolls) && lane == 0)
     atomicAdd(&g_timeouts, 1ull);
   if (cw == 0 && lane == 0) TRACE(tslot, 6);
+  // no CTA of the cluster leaves while the leader's shared memory may still
+  // receive partial sums
+  if constexpr (CL) cluster_sync_all();
 }
 
 // Shared-memory plan for M tokens and K; stages == 0 means "not applicable".
@@ -607,16 +693,17 @@ static bool try_plan(Plan& pl, int64_t x_bytes, int64_t K, int want, int64_t bud
   return false;
 }
 
-Plan plan(int64_t M, int64_t N, int64_t K, int co = 0, int gridx = 1) {
+Plan plan(int64_t M, int64_t N, int64_t K, int co = 0, int gridx = 1, int64_t extra_static = 0,
+          int64_t min_copy = 0) {
   Plan pl = {};
   if (M < 1 || M > 16 || K % 64 != 0 || K <= 0 || N <= 0 || K > (1 << 20)) return pl;
   const int nt = M <= 8 ? 1 : 2;
   if (co && nt != 1) return pl;
   // the static reduction array grows with the token groups (8 KB each)
-  const int64_t budget = co ? kCoSmemPerCta - 9 * 1024 : kSmemBudget - (nt - 1) * 8 * 1024;
+  const int64_t budget = (co ? kCoSmemPerCta - 9 * 1024 : kSmemBudget - (nt - 1) * 8 * 1024) - extra_static;
   // two CTAs per SM: row pieces of at least 2 KB (16 copies of 1 KB per slab
   // measured 1.4-2x slower), and no two-slab plan (x from L2 instead)
-  const int64_t mc = co ? 2048 : kMinRowCopy;
+  const int64_t mc = min_copy > 0 ? min_copy : co ? 2048 : kMinRowCopy;
   const int64_t xb = ((M * K * 2) + 127) / 128 * 128;
   // x in shared memory with three slabs; else x in tensor memory (when its
   // layout fits) with three slabs; else x in shared memory with two; else x
@@ -648,9 +735,10 @@ Plan plan(int64_t M, int64_t N, int64_t K, int co = 0, int gridx = 1) {
   return pl;
 }
 
-template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM = false, int CO = 0>
+template <typename InT, int FMT, int SCALE, typename OutT, int XM, int NT, bool NORM = false, int CO = 0,
+          bool CL = false>
 int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
-  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM, NT, NORM, CO>;
+  auto kern = gemv_bulk_kernel<InT, FMT, SCALE, OutT, XM, NT, NORM, CO, CL>;
   static cek_host::DeviceSlots configured_smem;
   // beside the static reduction array
   constexpr int kMaxDyn = CO ? kCoSmemPerCta - 9 * 1024 : kSmemBudget - (NT - 1) * 8 * 1024;
@@ -660,11 +748,18 @@ int launch(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = (size_t)pl.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (CL) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)pl.cl;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, kern, p, pl) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
 }
 
@@ -677,6 +772,10 @@ int launch_x(const GemvParams& p, const Plan& pl, cudaStream_t st) {
         if (pl.co) return launch<InT, F, S, OutT, kXSmem, NT, true, 1>(p, pl, st);
       return launch<InT, F, S, OutT, kXSmem, NT, true>(p, pl, st);
     }
+  if constexpr (F == CEK_E4M3 && NT == 1)
+    if (pl.cl > 1)
+      return pl.xmode == kXSmem ? launch<InT, F, S, OutT, kXSmem, NT, false, 1, true>(p, pl, st)
+                                : launch<InT, F, S, OutT, kXL2, NT, false, 1, true>(p, pl, st);
   if constexpr (F == CEK_E4M3 && NT == 1)
     if (pl.co)
       return pl.xmode == kXSmem   ? launch<InT, F, S, OutT, kXSmem, NT, false, 1>(p, pl, st)
@@ -708,6 +807,21 @@ int dispatch(const GemvParams& p, const Plan& pl, int w_fmt, int scale_kind, cud
 // does not fit it (more than 8 tokens or K % 64 != 0; the gated GeLU output
 // also needs a single matrix without the all-reduce push).  x and w must be
 // 16-byte aligned.
+// K-split clusters: only for long rows (K >= kMinClusterK) and clusters of at
+// least kMinCluster CTAs, in slices (and row pieces) of at least
+// kMinClusterSlice bytes; kClusterStatic is the static shared memory the split
+// adds (the leader's partial-sum array).  Measured (CUDA graph of calls over
+// cold weights, M = 1 / 2 / 4 / 8; without -> with the split):
+//   512 x 14336 (8 CTAs a cluster):  7.3 / 8.5 / 8.8 / 9.2 -> 6.5 / 6.8 / 6.9 / 6.7 us
+//   1024 x 14336 (4):                7.6 / 8.8 / 9.1 / 9.4 -> 7.1 / 7.3 / 7.7 / 7.9 us
+// and slower where the clusters are pairs or the rows shorter:
+//   2048 x 14336 (2): 8.8 -> 9.1 us at M = 1; 1280 x 8192 (2): 5.9 -> 6.9 us;
+//   640 x 8192 (4): 5.4 -> 5.4-5.8 us; 768 x 4096 (4, 1 KB slices): 3.9 -> 5.0 us.
+constexpr int64_t kMinClusterK = 12288;
+constexpr int kMinCluster = 4;
+constexpr int64_t kMinClusterSlice = 1024;
+constexpr int64_t kClusterStatic = 4 * 1024 + 64;
+
 int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, int scale_kind, cudaStream_t st) {
   static const bool disabled = [] {
     const char* v = std::getenv("CEK_GEMV_BULK");
@@ -726,6 +840,30 @@ int gemv_bulk_launch(const GemvParams& p, int x_dtype, int y_dtype, int w_fmt, i
     return g >= 1 && g <= 4 ? g : 2;
   }();
   bulk::Plan pl = {};
+  // Fewer 16-row blocks than SMs (a short shard) and long rows: split every
+  // row block along K over a cluster of C CTAs (the largest C in [4, 8] with
+  // K / C a multiple of 64 of at least kMinClusterSlice bytes and at most two
+  // CTAs per SM in all), two CTAs per SM.  CEK_BULK_CLUSTER=0 turns it off.
+  static const int cluster_mode = [] {
+    const char* v = std::getenv("CEK_BULK_CLUSTER");
+    return v ? std::atoi(v) : 1;
+  }();
+  const int64_t nrows0 = p.y_gelu ? 2 * (int64_t)p.N : p.N;
+  const int64_t nblk = (nrows0 + 15) / 16;
+  const int sms0 = cek_host::sm_count();
+  if (cluster_mode && w_fmt == CEK_E4M3 && !p.norm && !p.y_gelu && !p.nmat && p.M <= 8 && nblk < sms0 &&
+      p.K >= kMinClusterK && x_dtype == y_dtype) {
+    for (int c = bulk::kMaxCluster; c >= kMinCluster; --c) {
+      if (p.K % (64 * c) != 0 || p.K / c < kMinClusterSlice || nblk * c > 2 * (int64_t)sms0) continue;
+      // one row block per CTA: K pieces down to kMinClusterSlice bytes
+      bulk::Plan q = bulk::plan(p.M, nrows0, p.K / c, 1, 2, kClusterStatic, kMinClusterSlice);
+      if (q.stages == 0 || (q.xmode != bulk::kXSmem && q.xmode != bulk::kXL2)) continue;
+      q.cl = c;
+      q.grid = (int)(nblk * c);
+      return x_dtype == CEK_F16 ? bulk::dispatch<__half, __half>(p, q, w_fmt, scale_kind, st)
+                                : bulk::dispatch<__nv_bfloat16, __nv_bfloat16>(p, q, w_fmt, scale_kind, st);
+    }
+  }
   // ... when there are at least as many 16-row blocks as SMs: with fewer,
   // the grid is not two CTAs per SM anyway and the halved ring only costs
   // (e.g. one rank's down shard at 4- and 8-way tensor parallelism, 512 or

@@ -23,7 +23,8 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev)
-    cases = [(1, 6144, 4096), (8, 4096, 14336), (3, 1000, 512), (16, 2048, 1024)]
+    # the last case's shards (1024 rows of K = 14336) take the cluster K split
+    cases = [(1, 6144, 4096), (8, 4096, 14336), (3, 1000, 512), (16, 2048, 1024), (8, 2048, 14336)]
     ybytes = [M * N * 2 for M, N, K in cases]
     offs = [sum(ybytes[:i]) for i in range(len(cases))]
     total = (sum(ybytes) + 255) // 256 * 256

@@ -72,8 +72,12 @@ def test_column_parallel_reassembly_gloo():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (8, 4096, 14336), (5, 1000, 512), (20, 2048, 1024)])
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (8, 4096, 14336), (5, 1000, 512), (20, 2048, 1024),
+                                   (4, 2048, 14336), (1, 1024, 14336)])
 def test_allgather_push_two_regions_one_gpu(ext, cuda_device, M, N, K):
+    """Both ranks' shards pushed into two comm regions on one GPU; the last
+    two shapes' shards (1024 and 512 rows of K = 14336) take the cluster K
+    split, whose leader CTAs run the push epilogue."""
     import ctypes
     from esimd_learning_b200 import cabi
     L = cabi.lib()

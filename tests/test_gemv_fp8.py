@@ -183,6 +183,37 @@ def test_bulk_path_shapes(cuda_device, M, N, K, io, flags):
     assert n.value == 0
 
 
+@pytest.mark.parametrize("flags", FLAGS)
+@pytest.mark.parametrize("M,N,K", [(1, 512, 14336), (8, 512, 14336), (1, 1024, 14336), (4, 1, 16384),
+                                   (6, 333, 28672), (3, 700, 12288), (8, 1184, 14336), (2, 100, 14336),
+                                   (5, 1280, 8192), (7, 40, 8192), (3, 768, 4096)])
+@pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("per_tensor", [False, True])
+def test_cluster_k_split_shapes(cuda_device, M, N, K, io, flags, per_tensor):
+    """Shapes with fewer 16-row blocks than SMs and K >= 12288 take the
+    cluster K split (4-8 CTAs per row block, 6 at K = 12288, partial sums
+    reduced in the leader's shared memory): short shards of tensor-parallel
+    weights, ragged last blocks, N = 1; the last three shapes stay on the
+    plain bulk path.  Against the oracle; no bounded
+    wait may give up; two calls agree bit for bit."""
+    import ctypes
+    x, wq, s = gemv_case(M, N, K, seed=M * 104729 + N, dtype=io)
+    if per_tensor:
+        s = s[:1].clone()
+    xd, wd, sd = x.to(cuda_device), wq.to(cuda_device), s.to(cuda_device)
+    y = torch.full((M, N), float("nan"), dtype=io, device=cuda_device)
+    cabi_gemv(xd, wd, sd, y, per_tensor=per_tensor, flags=flags)
+    y2 = torch.full((M, N), float("nan"), dtype=io, device=cuda_device)
+    cabi_gemv(xd, wd, sd, y2, per_tensor=per_tensor, flags=flags)
+    torch.cuda.synchronize()
+    ref = O.gemv_fp8(x, wq, s)
+    O.assert_parity(y, ref, f"M={M} N={N} K={K}")
+    assert torch.equal(y, y2)
+    n = ctypes.c_uint64(99)
+    cabi.call("cek_gemv_fp8_timeouts", ctypes.byref(n))
+    assert n.value == 0
+
+
 def test_mixed_io_dtypes_cabi(cuda_device):
     """The C ABI allows input and output dtypes to differ (the reference host
     code instantiates all four combinations, fp8_GEMV_v2.h:181-190)."""

@@ -59,8 +59,13 @@ struct Tile {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + Q_BYTES;
   // warps: 0 TMA producer, 1 MMA, 2-5 epilogue, 6-9 converters (W8 kinds)
   static constexpr int THREADS = (is_w8(KIND) ? 10 : 6) * 32;
-  static constexpr int STAGES = (kSmemBudget - 2048) / STAGE_BYTES > 6 ? 6 : (kSmemBudget - 2048) / STAGE_BYTES;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  // The e4m3 kind stores its output through shared memory with TMA: one
+  // 32-row x 16-column staging buffer (1 KB) per epilogue warp, after the ring.
+  static constexpr bool TSTORE = KIND == kE4M3;
+  static constexpr int EPI_BYTES = TSTORE ? 4 * 1024 : 0;
+  static constexpr int STAGES = (kSmemBudget - 2048 - EPI_BYTES) / STAGE_BYTES > 6
+                                    ? 6 : (kSmemBudget - 2048 - EPI_BYTES) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024;  // + alignment slack
   // fp32 accumulate (bit 4), A/B format (bits 7-9 / 10-12: e4m3 = 0 for
   // kind::f8f6f4; f16 = 0, bf16 = 1 for kind::f16), both K-major, N = BN, M = 128
   static constexpr uint32_t FMT = mma_kind(KIND) == kBF16 ? 1u : 0u;
@@ -104,6 +109,14 @@ CEK_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, 
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
 }
+// TMA tensor store of a staged tile (bulk-group completion), and its waits
+CEK_DEVICE void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(map), "r"(x), "r"(y), "r"(src) : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+CEK_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+CEK_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 CEK_DEVICE void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 CEK_DEVICE void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -163,7 +176,7 @@ struct Params {
 template <typename OutT, int BN, int KIND, int WFMT = 0>
 __global__ void __launch_bounds__(Tile<BN, KIND>::THREADS, 1)
 gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                const Params p) {
+                const __grid_constant__ CUtensorMap map_y, const Params p) {
   using TL = Tile<BN, KIND>;
   constexpr int STAGES = TL::STAGES, STAGE_BYTES = TL::STAGE_BYTES, A_BYTES = TL::A_BYTES, B_BYTES = TL::B_BYTES;
   constexpr bool W8 = is_w8(KIND);
@@ -335,7 +348,26 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
           const float bs0 = __shfl_sync(0xffffffffu, bsv, 2 * i), bs1 = __shfl_sync(0xffffffffu, bsv, 2 * i + 1);
           o[i] = pack2<OutT>(__uint_as_float(r[2 * i]) * as * bs0, __uint_as_float(r[2 * i + 1]) * as * bs1);
         }
-        if (rv && n0 < p.N) {
+        if constexpr (TL::TSTORE) {
+          // Through shared memory: lane l writes its row's 16 columns (32 B)
+          // at l * 32 of the warp's buffer, then one lane stores the 32 x 16
+          // box with TMA (rows >= M are clipped by the tensor map; n0 is a
+          // multiple of 16 and N % 16 == 0, so a box is all in or all out).
+          // A row per lane over 16-byte stores would touch 32 lines a store.
+          const uint32_t buf = saddr(smem + STAGES * STAGE_BYTES + quad * 1024);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (lane == 0) bulk_wait_read_all();  // the previous box has left the buffer
+            __syncwarp();
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(buf + lane * 32), "r"(o[8 * h]),
+                         "r"(o[8 * h + 1]), "r"(o[8 * h + 2]), "r"(o[8 * h + 3]) : "memory");
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(buf + lane * 32 + 16), "r"(o[8 * h + 4]),
+                         "r"(o[8 * h + 5]), "r"(o[8 * h + 6]), "r"(o[8 * h + 7]) : "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0 && n0 + 16 * h < p.N) tma_store_2d(&map_y, buf, n0 + 16 * h, mb * BM + quad * 32);
+          }
+        } else if (rv && n0 < p.N) {
           uint4* dst = reinterpret_cast<uint4*>(yrow + n0);
           dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
           dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
@@ -349,6 +381,8 @@ gemm_fp8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant
       __syncwarp();
       if (lane == 0) bar_arrive(saddr(&acc_empty[b]));
     }
+    // every staged box written out before the CTA (and its shared memory) ends
+    if (TL::TSTORE && lane == 0) bulk_wait_all();
   }
 
   fence_before();
@@ -668,7 +702,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
 }
 
 template <typename OutT, int BN, int KIND, int WFMT = 0>
-int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaStream_t st) {
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& my, const Params& p, cudaStream_t st) {
   auto kern = gemm_fp8_kernel<OutT, BN, KIND, WFMT>;
   constexpr int SMEM_BYTES = Tile<BN, KIND>::SMEM_BYTES;
   static cek_host::DeviceSlots attr_set;
@@ -685,7 +719,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = cek_host::pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, ma, mb, p) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, my, p) == cudaSuccess ? CEK_OK : CEK_ERR_LAUNCH;
 }
 
 template <typename OutT, int BN>
@@ -775,11 +809,15 @@ int run_pair(const void* a, const void* b, const float* a_scale, const float* b_
   return CEK_ERR_UNSUPPORTED;
 }
 
-int choose_bn(int64_t M, int64_t N) {
-  // Tile N: the candidate that minimises (rounds of tiles over the SMs) x BN,
-  // i.e. the persistent grid's critical path.  A narrower tile must win by
-  // more than 3 %: per FLOP it is slightly slower (measured: at M = 8192,
-  // N = 14336 BN = 256 beats 224 although its cost is 2 % higher).
+int choose_bn(int64_t M, int64_t N, bool e4m3) {
+  // Tile N for the e4m3 kind: the candidate with the fewest rounds of tiles
+  // over the SMs, the widest on a tie.  Its tiles cost about the same whatever
+  // their width (per 128-byte k-block ~0.41 us at K = 4096, measured at
+  // M = 2048 / 8192: 13-14.4 us a tile for BN = 160-256), so only the rounds
+  // count: at M = 2048, N = 14336 BN = 256 (7 rounds, the last nearly empty)
+  // 99.3 us, 224 (7 rounds) 100.8, 192 (9) 117.3, 160 (10) 129.5.
+  // The 16-bit kinds minimise rounds x BN, a narrower tile having to win by
+  // more than 3 %.
   const int sms = cek_host::sm_count();
   const int64_t num_m = (M + BM - 1) / BM;
   const int cands[4] = {256, 224, 192, 160};
@@ -787,8 +825,13 @@ int choose_bn(int64_t M, int64_t N) {
   int64_t best = INT64_MAX / 100;
   for (int c : cands) {
     const int64_t tiles = num_m * ((N + c - 1) / c);
-    const int64_t cost = ((tiles + sms - 1) / sms) * c;
-    if (cost * 100 < best * 97) { best = cost; bn = c; }
+    const int64_t rounds = (tiles + sms - 1) / sms;
+    if (e4m3) {
+      if (rounds < best) { best = rounds; bn = c; }
+    } else if (rounds * c * 100 < best * 97) {
+      best = rounds * c;
+      bn = c;
+    }
   }
   static const int bn_env = [] {  // CEK_GEMM_BN forces the tile N (tuning only)
     const char* v = std::getenv("CEK_GEMM_BN");
@@ -802,12 +845,15 @@ int choose_bn(int64_t M, int64_t N) {
 template <int KIND, int WFMT = 0>
 int run(const void* a, const void* b, const float* a_scale, const float* b_scale, bool b_scalar, void* y,
         int64_t M, int64_t N, int64_t K, int eb, int y_dtype, cudaStream_t st) {
-  const int bn = choose_bn(M, N);
+  const int bn = choose_bn(M, N, KIND == kE4M3);
   CUtensorMap ma, mb;
   // W8 kinds: b is the FP8 weight, copied as dense 64-byte x bn boxes (one
   // k-block of 64 elements) into the staging tile
   const bool bmap = is_w8(KIND) ? make_map(&mb, b, N, K, bn, 1, 64, true) : make_map(&mb, b, N, K, bn, eb);
   if (!make_map(&ma, a, M, K, BM, eb) || !bmap) return CEK_ERR_LAUNCH;
+  // the output's map (e4m3 kind): 16-bit elements, 16 x 32 boxes, no swizzle
+  CUtensorMap my = ma;
+  if (Tile<256, KIND>::TSTORE && !make_map(&my, y, M, N, 32, 2, 32, true)) return CEK_ERR_LAUNCH;
   Params p;
   p.a_scale = a_scale; p.b_scale = b_scale; p.y = y;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
@@ -817,8 +863,8 @@ int run(const void* a, const void* b, const float* a_scale, const float* b_scale
   p.kblock_elems = BK / eb;
   p.b_scalar = b_scalar ? 1 : 0;
 #define CEK_GEMM_BN(B)                                                                        \
-  if (bn == B) return y_dtype == CEK_F16 ? launch<__half, B, KIND, WFMT>(ma, mb, p, st)      \
-                                         : launch<__nv_bfloat16, B, KIND, WFMT>(ma, mb, p, st);
+  if (bn == B) return y_dtype == CEK_F16 ? launch<__half, B, KIND, WFMT>(ma, mb, my, p, st)      \
+                                         : launch<__nv_bfloat16, B, KIND, WFMT>(ma, mb, my, p, st);
   CEK_GEMM_BN(256) CEK_GEMM_BN(224) CEK_GEMM_BN(192) CEK_GEMM_BN(160)
 #undef CEK_GEMM_BN
   return CEK_ERR_UNSUPPORTED;

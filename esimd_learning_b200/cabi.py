@@ -59,6 +59,7 @@ SIGNATURES = {
     "cek_gemm_fp8_scaled": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "cek_gemm_fp8w_workspace_bytes": (_I64, [_I64, _I64]),
     "cek_gemm_fp8w": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P]),
+    "cek_gemm_fp8w_preferred": (_I, [_I64, _I64, _I64]),
     "cek_gemv_fp8_timeouts": (_I, [ctypes.POINTER(ctypes.c_uint64)]),
     "cek_gemm_fp8_timeouts": (_I, [ctypes.POINTER(ctypes.c_uint64)]),
 }

@@ -923,7 +923,27 @@ extern "C" int64_t cek_gemm_fp8w_workspace_bytes(int64_t N, int64_t K) {
 // runs.  Measured at N = 14336, K = 4096: in-kernel 34.9 / 46.6 / 86.0 us at
 // M = 128 / 256 / 512 against 61.9 / 64.7 / 87.2 us dequantise-first, and
 // 283 against 206 us at M = 2048.
-constexpr int64_t kGemmW8MaxRows = 256;
+constexpr int64_t kGemmW8MaxRows = CEK_GEMM_FP8W_INKERNEL_MAX_ROWS;
+
+// GEMV family or this GEMM for 17..256 tokens, by estimated time (B200, CUDA
+// graph of calls over cold weights, per-tensor scale):
+//  * GEMV family: ~1.55e-8 us per weight byte per token + 8 us (14336 x 4096:
+//    M = 32 / 64 / 128 took 35.3 / 62.5 / 118.5 us; 6144 x 4096: 21.4 / 36.8
+//    / 67.0 us);
+//  * this GEMM: rounds of its 128 x 256 tiles over the SMs x 7.8 us per 1024
+//    of K (14336 x 4096: 32 us at any M in 17..128; 6144 x 4096: 31 us;
+//    4096 x 14336, 16 tiles on 16 SMs: 95 us at any M).
+// So 14336 x 4096 moves to the GEMM from M = 26, 6144 x 4096 from M = 60 and
+// 4096 x 14336 from M = 112 (28672 x 4096 from M = 17).
+extern "C" int cek_gemm_fp8w_preferred(int64_t M, int64_t N, int64_t K) {
+  if (M <= 16 || N <= 0 || K <= 0 || K % 64 != 0 || N % 16 != 0) return 0;
+  if (M > kGemmW8MaxRows) return 1;
+  const int64_t sms = cek_host::sm_count();
+  const int64_t tiles = ((M + 127) / 128) * ((N + 255) / 256);
+  const double gemm_us = (double)((tiles + sms - 1) / sms) * 7.8 * (double)K / 1024.0;
+  const double gemv_us = 1.55e-8 * (double)N * (double)K * (double)M + 8.0;
+  return gemm_us < gemv_us ? 1 : 0;
+}
 
 extern "C" int cek_gemm_fp8w(const void* x, const void* w, const void* scale, void* y, void* workspace,
                              int64_t workspace_bytes, int64_t M, int64_t N, int64_t K, int dtype, int w_fmt,

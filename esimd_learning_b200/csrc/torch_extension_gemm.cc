@@ -9,16 +9,14 @@ using namespace cek_torch;
 
 // Reference: esimd_gemm_fp8_pert (csrc/xpu/esimd_kernel_gemm.sycl:23-64).
 // bf16 I/O runs natively (the reference converts through fp16 copies,
-// esimd_kernel_gemm.sycl:45-48,61-63).  Decode sizes (M <= 64) run the
-// tensor-core GEMV family: one weight pass per 16-token tile, the tiles of
-// one row group scheduled next to each other so re-reads hit L2.  Prefill
-// sizes (M > 64, K % 64 == 0, N % 16 == 0) run the tcgen05 GEMM with the
-// weight converted exactly to 16 bits (cek_gemm_fp8w: in shared memory up to
-// 256 tokens, into a workspace first above that).
-// Token count above which the per-tensor GEMM leaves the GEMV family for the
-// tcgen05 GEMM (the reference's own decode/prefill split,
-// csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4043-4048).
-constexpr int64_t kGemmMinRows = 64;
+// esimd_kernel_gemm.sycl:45-48,61-63).  The reference splits decode (M <= 64,
+// GEMV) from prefill (GEMM) at a fixed token count
+// (csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4043-4048); here
+// cek_gemm_fp8w_preferred picks by estimated time: the tensor-core GEMV
+// family (one weight pass per 16-token tile) for few tokens or few output
+// tiles, else the tcgen05 GEMM with the weight converted exactly to 16 bits
+// (cek_gemm_fp8w: in shared memory up to 256 tokens, into a workspace first
+// above that).
 
 at::Tensor esimd_gemm_fp8_pert(at::Tensor input, at::Tensor weight, at::Tensor weight_scale,
                                at::Tensor output) {
@@ -40,13 +38,14 @@ at::Tensor esimd_gemm_fp8_pert(at::Tensor input, at::Tensor weight, at::Tensor w
   TORCH_CHECK(output.numel() == M * N, op, ": output must be [M, N]");
   const int fmt = fp8_format(weight, op);
   c10::cuda::CUDAGuard guard(input.device());
-  if (M > kGemmMinRows && K % 64 == 0 && N % 16 == 0 && input.is_contiguous() && output.is_contiguous() &&
+  if (cek_gemm_fp8w_preferred(M, N, K) && input.is_contiguous() && output.is_contiguous() &&
       weight.is_contiguous()) {
-    const int64_t ws_bytes = cek_gemm_fp8w_workspace_bytes(N, K);
-    at::Tensor ws = at::empty({ws_bytes}, input.options().dtype(at::kByte));
+    // the 16-bit weight copy is needed only above the in-kernel conversion's rows
+    const int64_t ws_bytes = M > CEK_GEMM_FP8W_INKERNEL_MAX_ROWS ? cek_gemm_fp8w_workspace_bytes(N, K) : 0;
+    at::Tensor ws = ws_bytes ? at::empty({ws_bytes}, input.options().dtype(at::kByte)) : at::Tensor();
     check_status(cek_gemm_fp8w(input.data_ptr(), weight.data_ptr(), weight_scale.data_ptr(), output.data_ptr(),
-                               ws.data_ptr(), ws_bytes, M, N, K, io_dtype(input), fmt, CEK_SCALE_PERT_F32,
-                               stream_of(input)),
+                               ws_bytes ? ws.data_ptr() : nullptr, ws_bytes, M, N, K, io_dtype(input), fmt,
+                               CEK_SCALE_PERT_F32, stream_of(input)),
                  op);
     return output;
   }

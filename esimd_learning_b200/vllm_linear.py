@@ -9,11 +9,13 @@ e5m2) with an fp32 ``weight_scale``, per output channel [N] or per tensor
 [1].  ``apply`` keeps the activations in fp16/bf16, which is the reference
 ops' arithmetic (no activation quantisation):
 
-* M <= 64 tokens: the GEMV family (``esimd_gemv_fp8_pern``, the bulk-copy
-  kernel for M <= 16): one weight pass per 16-token tile;
-* M > 64 (prefill): ``cek_gemm_fp8w``, a ``kind::f16`` tcgen05 GEMM on the
-  weight converted exactly to 16 bits (in shared memory up to 256 tokens,
-  into a workspace taken from the caching allocator for the call above), the
+* few tokens (``cek_gemm_fp8w_preferred`` false: always for M <= 16, and
+  up to M = 25 / 59 / 111 for 14336 x 4096 / 6144 x 4096 / 4096 x 14336):
+  the GEMV family (``esimd_gemv_fp8_pern``, the bulk-copy kernel for
+  M <= 16), one weight pass per 16-token tile;
+* otherwise ``cek_gemm_fp8w``, a ``kind::f16`` tcgen05 GEMM on the weight
+  converted exactly to 16 bits (in shared memory up to 256 tokens, into a
+  workspace taken from the caching allocator for the call above), the
   scale in its epilogue.  K % 64 == 0 and N % 16 == 0 are needed; other
   shapes stay on the GEMV family.
 
@@ -23,8 +25,7 @@ from __future__ import annotations
 
 import torch
 
-GEMV_MAX_TOKENS = 64
-GEMM_W8_MAX_TOKENS = 256  # cek_gemm_fp8w converts weight tiles in shared memory up to this M
+GEMM_W8_MAX_TOKENS = 256  # CEK_GEMM_FP8W_INKERNEL_MAX_ROWS: no workspace up to this M
 
 
 class EsimdFp8LinearMethod:
@@ -75,7 +76,7 @@ class EsimdFp8LinearMethod:
         y = torch.empty(M, N, dtype=x.dtype, device=x.device)
         if M == 0:
             return y.reshape(*lead, N)
-        if M > GEMV_MAX_TOKENS and K % 64 == 0 and N % 16 == 0:
+        if cabi.lib().cek_gemm_fp8w_preferred(M, N, K):
             # the 16-bit weight copy is needed only above GEMM_W8_MAX_TOKENS
             nb = cabi.lib().cek_gemm_fp8w_workspace_bytes(N, K) if M > GEMM_W8_MAX_TOKENS else 0
             ws = torch.empty(nb, dtype=torch.uint8, device=x.device) if nb else None

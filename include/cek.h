@@ -292,6 +292,20 @@ CEK_API int64_t cek_gemm_fp8w_workspace_bytes(int64_t N, int64_t K);
 CEK_API int cek_gemm_fp8w(const void* x, const void* w, const void* scale, void* y,
                           void* workspace, int64_t workspace_bytes, int64_t M, int64_t N,
                           int64_t K, int dtype, int w_fmt, int scale_kind, void* stream);
+/* Up to this many tokens cek_gemm_fp8w converts the weight in shared memory
+ * and never touches the workspace (null with 0 bytes is accepted). */
+#define CEK_GEMM_FP8W_INKERNEL_MAX_ROWS 256
+
+/* 1 when a 16-bit-activation FP8-weight product of M tokens should run on
+ * cek_gemm_fp8w rather than the GEMV family (cek_gemv_fp8), else 0.  It
+ * replaces the fixed decode/prefill cut of the reference's
+ * GEMM_fp8_pert_dispatch (csrc/xpu/esimd_kernels/fp8_GEMM_pert.h:4043-4048,
+ * M > 64 to the GEMM) with a time estimate from measurements on B200: the
+ * GEMV family streams the weight once per 16-token tile, the GEMM once per
+ * 128-row block but on no more CTAs than it has 128 x 256 tiles.  Always 0
+ * for M <= 16 or shapes the GEMM does not take (K % 64, N % 16), always 1
+ * above CEK_GEMM_FP8W_INKERNEL_MAX_ROWS.  Host only, no device work. */
+CEK_API int cek_gemm_fp8w_preferred(int64_t M, int64_t N, int64_t K);
 
 /* Number of bounded device waits in the bulk-copy GEMV kernel (the
  * cek_gemv_fp8 path for up to 16 tokens) that gave up since the library was

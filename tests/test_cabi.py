@@ -68,3 +68,18 @@ def test_norm_and_helpers_reject_bad_arguments():
     assert L.cek_qkv_norm_rope(16, 16, 16, 16, 16, 1, 8, 1, 96, 64, 1e-6, 1, 0,
                                None) == cabi.CEK_ERR_INVALID_ARG
     assert L.cek_quant_fp8_per_token(16, 16, 16, 1, 12, 0, None) == cabi.CEK_ERR_INVALID_ARG
+
+
+def test_gemm_fp8w_preferred_crossovers():
+    """The per-tensor dispatch (host only, no device work): GEMV family for
+    M <= 16 and shapes the GEMM does not take, the tcgen05 GEMM above 256
+    tokens, and in between the measured crossovers (148 SMs)."""
+    L = cabi.lib()
+    pref = L.cek_gemm_fp8w_preferred
+    assert pref(16, 28672, 4096) == 0 and pref(17, 28672, 4096) == 1
+    assert pref(25, 14336, 4096) == 0 and pref(26, 14336, 4096) == 1
+    assert pref(59, 6144, 4096) == 0 and pref(60, 6144, 4096) == 1
+    assert pref(111, 4096, 14336) == 0 and pref(112, 4096, 14336) == 1
+    assert pref(257, 16, 64) == 1 and pref(300, 4096, 14336) == 1
+    assert pref(64, 14336, 4100) == 0 and pref(64, 14348, 4096) == 0
+    assert pref(0, 14336, 4096) == 0 and pref(64, 0, 4096) == 0

@@ -41,7 +41,9 @@ def test_gemm_pert_correctness(ext, cuda_device, N, K, wdt, io):
 
 
 @pytest.mark.parametrize("M,N,K", [(65, 256, 512), (128, 512, 256), (300, 1040, 384), (257, 2048, 2048),
-                                   (1000, 4096, 1024)])
+                                   (1000, 4096, 1024),
+                                   # either side of cek_gemm_fp8w_preferred's crossovers
+                                   (25, 14336, 4096), (26, 14336, 4096), (111, 4096, 14336), (112, 4096, 14336)])
 @pytest.mark.parametrize("wdt", [torch.float8_e4m3fn, torch.float8_e5m2])
 @pytest.mark.parametrize("io", [torch.float16, torch.bfloat16])
 def test_gemm_pert_prefill(ext, cuda_device, M, N, K, wdt, io):
